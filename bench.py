@@ -1,0 +1,405 @@
+#!/usr/bin/env python
+"""FWLoss forward+backward throughput on B200 (rows/s, HBM roofline).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config cfgX]
+
+Default workload: cfg2 of the reference's benchmark set -- B=4096 rows x
+C=32000 classes, fp32 Student-t(3)*2 logits, int64 labels (seeded synthetic
+data, fwloss_b200.workloads).  A step is one fused forward+backward of the
+whole batch (threshold search, per-row loss, dense gradient) plus the
+deterministic loss reduction; with N > 1 ranks each rank runs its own batch
+of B rows (weak scaling, rows are independent) and the global mean is
+combined by one scalar NCCL all-reduce.
+
+Printed JSON line (rank 0):
+  value     rows/s of the whole job, inputs resident in HBM, device-timed with
+            CUDA events over exactly K steps (barrier + synchronize on both
+            sides, max over ranks).
+  e2e       same metric through the public autograd API with the logits and
+            labels copied from pinned host memory every step and the loss read
+            back (host<->device copies inside the timed region).
+  roofline  the fused kernel alone: algorithmic bytes per launch
+            (B * (8C + 12): read logits, write gradient, label, loss) over its
+            CUDA-event average duration, against the measured HBM copy peak.
+  cpu_baseline  the reference's own CPU implementation (src/cpu/fw_cpu.cpp,
+            compiled by oracle/build.py) on this host's cores, on a bounded
+            sample of the same workload (rank 0, N = 1 only).
+--impl reference runs only that CPU implementation (the reference arm).
+"""
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG_ROOT = os.path.join(REPO, "fast-familywise-loss_b200")
+for _p in (REPO, PKG_ROOT):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "FWLoss fwd+bwd rows/s & HBM GB/s vs peak, B=4096 C=32000, 1/2/4/8 B200"
+UNIT = "rows/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--config", default="cfg2")
+    p.add_argument("--e2e-steps", type=int, default=0, help="0: min(steps, 10)")
+    p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample budget")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def workload_desc(name, B, C, world):
+    kinds = {"cfg0": "N(0,1)", "cfg1": "N(0,1) +4 at label", "cfg2": "Student-t(3) x2",
+             "cfg3": "8 levels + 1% signed zeros", "cfg4": "N(0,1) +8 at a non-label class"}
+    return {
+        "workload": f"{name}: FWLoss fwd+bwd, B={B} x C={C}, fp32 logits {kinds.get(name, '')}, int64 labels",
+        "rows_per_gpu": B, "classes": C, "global_batch": B * world,
+        "parallelism": f"row-sharded dp{world}" + (" + scalar NCCL all-reduce" if world > 1 else ""),
+        "l2": f"inputs {B * C * 4 / 1e6:.0f} MB logits + {B * C * 4 / 1e6:.0f} MB gradient per step"
+              + (" (> 126 MB L2, no flush needed)" if B * C * 4 > 126e6 else " (< L2: 4 rotating input copies)"),
+    }
+
+
+def measured_peak():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic(name):
+    """DRAM bytes per launch of the fused kernel from the committed ncu summary."""
+    try:
+        with open(os.path.join(REPO, "profiles", "traffic.json")) as f:
+            return json.load(f).get(name)
+    except (OSError, ValueError):
+        return None
+
+
+class Clocks:
+    """nvidia-smi sampler (200 ms) around the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, phys_index):
+        self.idx = phys_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.idx), "-lms", "200", "-f", self.path],
+                                         stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        sm, mx, reasons = [], [], set()
+        try:
+            lines = open(self.path).read().strip().splitlines()
+        except OSError:
+            lines = []
+        for ln in lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        try:
+            os.unlink(self.path)
+        except OSError:
+            pass
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline(name, B, C, seconds):
+    """The reference CPU implementation (or the C restatement) on a bounded
+    sample of the workload; returns the cpu_baseline object."""
+    import torch
+    from fwloss_b200 import workloads
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    rows = min(B, 1024)
+    z, y = workloads.make(name, rows=rows)
+    try:
+        from oracle import ref_cpu
+
+        mod = ref_cpu.ref_module()
+        kind = "reference"
+
+        def step():
+            Z = z.clone().requires_grad_(True)
+            mod.familywise_loss(Z, y, 1).backward()
+    except ImportError:
+        from oracle import ref_cpu
+
+        kind = "port"
+        zn, yn = z.numpy(), y.numpy()
+
+        def step():
+            ref_cpu.c_solve(zn, yn, threads)
+    step()
+    n, t0 = 0, time.perf_counter()
+    while True:
+        step()
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return {"value": rows * n / el, "unit": UNIT, "cores": threads, "kind": kind,
+            "sample": f"{rows} rows of {name} (C={C}) per call, {n} calls in {el:.1f} s, "
+                      f"familywise_loss(..., mean).backward()" if kind == "reference" else
+                      f"{rows} rows of {name} per call, {n} calls in {el:.1f} s (C restatement)"}
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import torch
+    from fwloss_b200 import workloads
+
+    B, C = workloads.CONFIGS[a.config]
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    from oracle import ref_cpu
+
+    mod = ref_cpu.ref_module()
+    z, y = workloads.make(a.config)
+
+    def step(zz, yy):
+        Z = zz.clone().requires_grad_(True)
+        mod.familywise_loss(Z, yy, 1).backward()
+
+    # bounded sample: shrink the rows per step if one full step is slow
+    t = time.perf_counter()
+    step(z, y)
+    one = time.perf_counter() - t
+    rows = B if one * (a.steps + a.warmup) < 120 else max(64, int(B * 120 / (one * (a.steps + a.warmup))))
+    zs, ys = z[:rows].contiguous(), y[:rows].contiguous()
+    for _ in range(a.warmup):
+        step(zs, ys)
+    t = time.perf_counter()
+    for _ in range(a.steps):
+        step(zs, ys)
+    el = time.perf_counter() - t
+    value = rows * a.steps / el
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": a.gpus,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * el / a.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": workload_desc(a.config, rows, C, 1),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
+                         "sample": f"{rows} rows of {a.config} per step (reference src/cpu/fw_cpu.cpp, "
+                                   f"familywise_loss mean + backward, simd={mod.simd()})"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(a):
+    import torch
+    import torch.distributed as dist
+
+    from fwloss_b200 import familywise_loss, workloads
+    from fwloss_b200._native import ext
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.gpus != world and world > 1:
+        print(f"warning: --gpus {a.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    B, C = workloads.CONFIGS[a.config]
+    fw = ext()
+
+    # inputs: rank 0 gets the configuration itself, other ranks the same recipe
+    # with their own seed (weak scaling: every rank owns B distinct rows)
+    z_cpu, y_cpu = workloads.make_rank(a.config, rank)
+    copies = 1 if B * C * 4 > 126e6 else 4
+    zs = [z_cpu.to(dev) for _ in range(copies)]
+    y = y_cpu.to(dev)
+    Bg = B * world
+    scale = 1.0 / Bg
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        grad, H, loss, kappa = fw.fused_fwd_bwd(zs[i % copies], y, scale)
+        s = fw.loss_reduce(loss, scale)
+        if world > 1:
+            dist.all_reduce(s)
+        return s
+
+    for i in range(a.warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    phys = local
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        try:
+            phys = int(vis.split(",")[local])
+        except (ValueError, IndexError):
+            phys = local
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(phys) as clk:
+        barrier()
+        torch.cuda.synchronize(dev)
+        e0.record(stream)
+        for i in range(a.steps):
+            step(i)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+    ms = e0.elapsed_time(e1)
+    clocks = clk.summary()
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    value = Bg * a.steps / (ms / 1e3)
+
+    # roofline: the fused kernel alone, back to back on the launching stream
+    kd0, kd1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for i in range(3):
+        fw.fused_fwd_bwd(zs[i % copies], y, scale)
+    torch.cuda.synchronize(dev)
+    kd0.record(stream)
+    for i in range(a.steps):
+        fw.fused_fwd_bwd(zs[i % copies], y, scale)
+    kd1.record(stream)
+    torch.cuda.synchronize(dev)
+    k_ms = kd0.elapsed_time(kd1) / a.steps
+    alg_bytes = B * (8 * C + 12)
+    achieved = alg_bytes / (k_ms / 1e3) / 1e9
+    peak, peak_kind = measured_peak()
+
+    # e2e: public autograd API, host buffers, copies inside the timed region
+    ne = a.e2e_steps or min(a.steps, 10)
+    zh = z_cpu.pin_memory()
+    yh = y_cpu.pin_memory()
+    zd = torch.empty_like(zs[0]).requires_grad_(True)
+    yd = torch.empty_like(y)
+    lh = torch.empty(ne + a.warmup, dtype=torch.float32).pin_memory()
+
+    def e2e_step(i):
+        with torch.no_grad():
+            zd.copy_(zh, non_blocking=True)
+            yd.copy_(yh, non_blocking=True)
+        zd.grad = None
+        loss = familywise_loss(zd, yd, reduction="mean")
+        loss.backward()
+        if world > 1:
+            l2 = loss.detach().clone()
+            dist.all_reduce(l2)
+            loss = l2
+        lh[i:i + 1].copy_(loss.detach().reshape(1), non_blocking=True)
+
+    for i in range(min(2, a.warmup)):
+        e2e_step(i)
+    torch.cuda.synchronize(dev)
+    barrier()
+    ee0, ee1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ee0.record(stream)
+    for i in range(ne):
+        e2e_step(a.warmup + i)
+    ee1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e_ms = ee0.elapsed_time(ee1)
+    t = torch.tensor([e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e_ms = float(t.item())
+    e2e = {"value": Bg * ne / (e_ms / 1e3), "unit": UNIT,
+           "h2d_bytes_per_step": int(zh.numel() * 4 + yh.numel() * 8), "d2h_bytes_per_step": 4,
+           "ms_per_step": e_ms / ne, "api": "fwloss_b200.familywise_loss(mean).backward()"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        try:
+            cpu = cpu_baseline(a.config, B, C, a.cpu_seconds)
+        except Exception as ex:  # report, do not fail the GPU measurement
+            cpu = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "unavailable",
+                   "sample": f"failed: {ex!r}"[:200]}
+
+    if rank == 0:
+        launches_per_step = 2
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": ms / a.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_desc(a.config, B, C, world),
+            "hbm_gbs": alg_bytes * world * a.steps / (ms / 1e3) / 1e9 / world,
+            "roofline": {"bound": "hbm", "kernel": "fw_stream_rows_kernel" if C > 2048 else "fw_warp_rows_kernel",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_kind": peak_kind, "traffic": profile_traffic(a.config),
+                         "alg_bytes_per_launch": alg_bytes, "kernel_ms": k_ms},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": launches_per_step * a.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        return run_reference(a)
+    return run_ours(a)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,263 @@
+// C ABI of libfwloss_b200.so: argument checks, tier selection and launches.
+// Declarations and semantics: include/fwloss_b200.h.
+//
+// Tier selection by class count C (the tile shape scales with C):
+//   C <= 2048          warp per row, row in registers (fw_warp_tier.cuh);
+//                      VW = ceil(C / 128) 16-byte slots per lane.
+//   C  > 2048          CTA per row (CS = 1) or a cluster of CS = 2/4/8 CTAs per
+//                      row when there are too few rows to fill the GPU
+//                      (fw_stream_tier.cuh).
+// 128-bit loads/stores are used when every row starts on a 16-byte boundary
+// (base pointers 16-byte aligned and ld % 4 == 0); otherwise the same kernels
+// run with coalesced 32-bit accesses.
+#include <cuda_runtime.h>
+
+#include <climits>
+#include <cstdint>
+
+#include "../../include/fwloss_b200.h"
+#include "fw_aux.cuh"
+#include "fw_device.cuh"
+#include "fw_stream_tier.cuh"
+#include "fw_warp_tier.cuh"
+
+namespace fwb200 {
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr int64_t kWarpTierMaxC = 2048;
+
+int sm_count() {
+  static int cache[kMaxDevices] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 148;
+  if (dev < kMaxDevices && cache[dev] > 0) return cache[dev];
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+    n = 148;
+  if (dev < kMaxDevices) cache[dev] = n;
+  return n;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int launch_status(cudaError_t e) { return e == cudaSuccess ? FWB_OK : FWB_E_LAUNCH; }
+
+template <class... KArgs, class... Args>
+cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, int cluster,
+                   cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (cluster > 1) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// ------------------------------------------------------------- warp tier
+template <int VW, bool VEC, int OUT>
+cudaError_t launch_warp_tier(const RowArgs& a, cudaStream_t st) {
+  auto k = fw_warp_rows_kernel<VW, VEC, OUT>;
+  static int occ = 0;  // resident CTAs per SM for this instance
+  if (occ == 0) {
+    int o = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k, kWarpTierThreads, 0) != cudaSuccess || o < 1)
+      o = 1;
+    occ = o;
+  }
+  const int64_t need = (a.B + kWarpTierWarps - 1) / kWarpTierWarps;
+  const int64_t cap = (int64_t)sm_count() * occ;
+  const int grid = (int)(need < cap ? need : cap);
+  return launch(k, dim3(grid), dim3(kWarpTierThreads), 1, st, a);
+}
+
+template <bool VEC, int OUT>
+cudaError_t dispatch_warp_vw(const RowArgs& a, cudaStream_t st) {
+  const int64_t slots = (a.C + 127) / 128;
+  if (slots <= 1) return launch_warp_tier<1, VEC, OUT>(a, st);
+  if (slots <= 2) return launch_warp_tier<2, VEC, OUT>(a, st);
+  if (slots <= 4) return launch_warp_tier<4, VEC, OUT>(a, st);
+  if (slots <= 8) return launch_warp_tier<8, VEC, OUT>(a, st);
+  return launch_warp_tier<16, VEC, OUT>(a, st);
+}
+
+// ----------------------------------------------------------- stream tier
+template <int CS, bool VEC, int OUT>
+cudaError_t launch_stream_tier(const RowArgs& a, cudaStream_t st) {
+  auto k = fw_stream_rows_kernel<CS, VEC, OUT>;
+  const int64_t grid = a.B * CS;
+  return launch(k, dim3((unsigned)grid), dim3(kST), CS, st, a);
+}
+
+// Cluster size: the smallest CS in {1, 2, 4, 8} giving at least 4 CTAs per SM,
+// while every CTA keeps a segment of at least 4096 columns.
+int choose_cluster(int64_t B, int64_t C) {
+  const int64_t want = (int64_t)sm_count() * 4;
+  int cs = 1;
+  while (cs < 8 && B * cs < want && C / (cs * 2) >= 4096) cs *= 2;
+  return cs;
+}
+
+template <bool VEC, int OUT>
+cudaError_t dispatch_stream_cs(const RowArgs& a, cudaStream_t st) {
+  switch (choose_cluster(a.B, a.C)) {
+    case 8: return launch_stream_tier<8, VEC, OUT>(a, st);
+    case 4: return launch_stream_tier<4, VEC, OUT>(a, st);
+    case 2: return launch_stream_tier<2, VEC, OUT>(a, st);
+    default: return launch_stream_tier<1, VEC, OUT>(a, st);
+  }
+}
+
+template <int OUT>
+int run_rows(const RowArgs& a, cudaStream_t st, bool vec) {
+  if (a.B == 0) return FWB_OK;
+  cudaError_t e;
+  if (a.C <= kWarpTierMaxC)
+    e = vec ? dispatch_warp_vw<true, OUT>(a, st) : dispatch_warp_vw<false, OUT>(a, st);
+  else
+    e = vec ? dispatch_stream_cs<true, OUT>(a, st) : dispatch_stream_cs<false, OUT>(a, st);
+  return launch_status(e);
+}
+
+int check_shape(int64_t B, int64_t C, int64_t ld) {
+  if (B < 0 || C < 1 || ld < C) return FWB_E_SHAPE;
+  if (C > (int64_t)INT_MAX - 64) return FWB_E_SHAPE;         // int32 column indices
+  if (B > (int64_t)INT_MAX / 8) return FWB_E_SHAPE;          // grid of B * CS CTAs
+  if (B > 0 && ld > ((int64_t)1 << 62) / B) return FWB_E_SHAPE;
+  return FWB_OK;
+}
+
+RowArgs base_args(const float* z, const int64_t* y, int64_t B, int64_t C, int64_t ld,
+                  float* H, float* loss, int32_t* kappa, int32_t* status) {
+  RowArgs a = {};
+  a.z = z;
+  a.y = y;
+  a.B = B;
+  a.C = C;
+  a.ld = ld;
+  a.scale = 1.0f;
+  a.H = H;
+  a.loss = loss;
+  a.kappa = kappa;
+  a.status = status;
+  return a;
+}
+
+int aux_grid(int64_t rows, int per_block) {
+  const int64_t need = (rows + per_block - 1) / per_block;
+  const int64_t cap = (int64_t)sm_count() * 8;
+  const int64_t g = need < cap ? need : cap;
+  return (int)(g < 1 ? 1 : g);
+}
+
+}  // namespace
+}  // namespace fwb200
+
+using namespace fwb200;
+
+extern "C" {
+
+const char* fw_version(void) { return "0.1.0"; }
+
+const char* fw_error_string(int code) {
+  switch (code) {
+    case FWB_OK: return "ok";
+    case FWB_E_SHAPE: return "invalid shape (need B >= 0, 1 <= C < 2^31 - 64, ld >= C)";
+    case FWB_E_POINTER: return "a required pointer is NULL";
+    case FWB_E_LAUNCH: return "CUDA kernel launch failed";
+    case FWB_E_CAPACITY: return "size exceeds the stated maximum";
+    default: return "unknown error";
+  }
+}
+
+int fw_fused_fwd_bwd(const float* z, const int64_t* y, int64_t B, int64_t C, int64_t ld,
+                     float grad_scale, float* grad, float* H, float* loss, int32_t* kappa,
+                     int32_t* status, void* stream) {
+  if (int rc = check_shape(B, C, ld)) return rc;
+  if (B > 0 && (!z || !y || !grad)) return FWB_E_POINTER;
+  RowArgs a = base_args(z, y, B, C, ld, H, loss, kappa, status);
+  a.scale = grad_scale;
+  a.grad = grad;
+  const bool vec = aligned16(z) && aligned16(grad) && (ld % 4 == 0);
+  return run_rows<kOutGrad>(a, static_cast<cudaStream_t>(stream), vec);
+}
+
+int fw_forward_mask(const float* z, const int64_t* y, int64_t B, int64_t C, int64_t ld,
+                    float* H, float* loss, int32_t* kappa, uint8_t* mask, int32_t* status,
+                    void* stream) {
+  if (int rc = check_shape(B, C, ld)) return rc;
+  if (B > 0 && (!z || !y || !mask)) return FWB_E_POINTER;
+  RowArgs a = base_args(z, y, B, C, ld, H, loss, kappa, status);
+  a.mask = mask;
+  a.mask_vec = (C % 4 == 0) && ((reinterpret_cast<uintptr_t>(mask) & 3u) == 0);
+  const bool vec = aligned16(z) && (ld % 4 == 0);
+  return run_rows<kOutMask>(a, static_cast<cudaStream_t>(stream), vec);
+}
+
+int fw_backward_mask(const int64_t* y, const uint8_t* mask, const int32_t* kappa, int64_t B,
+                     int64_t C, float grad_scale, float* grad, int32_t* status, void* stream) {
+  if (int rc = check_shape(B, C, C)) return rc;
+  if (B == 0) return FWB_OK;
+  if (!y || !mask || !kappa || !grad) return FWB_E_POINTER;
+  const int vec = (C % 4 == 0) && aligned16(grad) && ((reinterpret_cast<uintptr_t>(mask) & 3u) == 0);
+  const int warps_per_block = kAuxThreads / 32;
+  return launch_status(launch(fw_backward_mask_kernel, dim3(aux_grid(B, warps_per_block)),
+                              dim3(kAuxThreads), 1, static_cast<cudaStream_t>(stream), y, mask,
+                              kappa, B, C, grad_scale, grad, status, vec));
+}
+
+int fw_forward_candidates(const float* z, const int64_t* y, int64_t B, int64_t C, int64_t ld,
+                          float* H, float* loss, int32_t* kappa, float* cand_val,
+                          int32_t* cand_idx, int32_t* cand_count, int32_t* status,
+                          void* stream) {
+  if (int rc = check_shape(B, C, ld)) return rc;
+  if (B > 0 && (!z || !y || !cand_val || !cand_idx)) return FWB_E_POINTER;
+  RowArgs a = base_args(z, y, B, C, ld, H, loss, kappa, status);
+  a.cand_val = cand_val;
+  a.cand_idx = cand_idx;
+  a.cand_count = cand_count;
+  const bool vec = aligned16(z) && (ld % 4 == 0);
+  return run_rows<kOutCand>(a, static_cast<cudaStream_t>(stream), vec);
+}
+
+int fw_backward_candidates(const float* cand_val, const int32_t* cand_idx,
+                           const int32_t* cand_count, const float* H, const int32_t* kappa,
+                           const int64_t* y, int64_t B, int64_t C, float grad_scale,
+                           float* grad, int32_t* status, void* stream) {
+  if (int rc = check_shape(B, C, C)) return rc;
+  if (B == 0) return FWB_OK;
+  if (!cand_val || !cand_idx || !cand_count || !H || !kappa || !y || !grad) return FWB_E_POINTER;
+  const int vec = (C % 4 == 0) && aligned16(grad);
+  return launch_status(launch(fw_backward_cand_kernel, dim3(aux_grid(B, 1)), dim3(kAuxThreads), 1,
+                              static_cast<cudaStream_t>(stream), cand_val, cand_idx, cand_count,
+                              H, kappa, y, B, C, grad_scale, grad, status, vec));
+}
+
+int fw_scale_grad(float* grad, const float* grad_output, int per_row, float assumed_scale,
+                  int64_t B, int64_t C, int64_t ld, void* stream) {
+  if (int rc = check_shape(B, C, ld)) return rc;
+  if (B == 0) return FWB_OK;
+  if (!grad || !grad_output) return FWB_E_POINTER;
+  const int vec = aligned16(grad) && (ld % 4 == 0);
+  return launch_status(launch(fw_scale_grad_kernel, dim3(aux_grid(B, 1)), dim3(kAuxThreads), 1,
+                              static_cast<cudaStream_t>(stream), grad, grad_output, per_row,
+                              assumed_scale, B, C, ld, vec));
+}
+
+int fw_loss_reduce(const float* loss, int64_t B, double scale, float* out, void* stream) {
+  if (B < 0) return FWB_E_SHAPE;
+  if (!out || (B > 0 && !loss)) return FWB_E_POINTER;
+  return launch_status(launch(fw_loss_reduce_kernel, dim3(1), dim3(kReduceThreads), 1,
+                              static_cast<cudaStream_t>(stream), loss, B, scale, out));
+}
+
+}  // extern "C"

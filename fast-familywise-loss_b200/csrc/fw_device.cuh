@@ -1,0 +1,159 @@
+// Device helpers shared by every FW-loss kernel: order-preserving keys,
+// NaN-propagating max, warp reductions and the exact threshold solver that
+// runs on a short candidate list.
+//
+// Notation used throughout (one row z[0..C), label y):
+//   M       row maximum (fp32, NaN if any element is NaN)
+//   t0      __fsub_rd(M, 1): the largest fp32 <= M - 1.  Because
+//           h* >= M - 1 (k = 1 in max_k (S_k - 1)/k), every support element
+//           satisfies z > t0, so {z > t0} is a superset of the support.
+//   d_j     (double)z_j - (double)M, the shifted logit (<= 0).  The search
+//           runs in the shifted domain, tau = h* - M, which keeps the
+//           arithmetic exact for magnitudes up to ~1e38 (z - M is exact for
+//           every candidate when M >= 2, Sterbenz) where the unshifted
+//           S_k - 1 would lose the 1 entirely.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <math_constants.h>
+#include <stdint.h>
+
+namespace fwb200 {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+// Output of the forward search: the gradient row, the support mask, or the
+// support as a (value, column) list.
+enum OutMode : int { kOutGrad = 0, kOutMask = 1, kOutCand = 2 };
+
+struct RowArgs {
+  const float* z;        // [B, ld]
+  const int64_t* y;      // [B]
+  int64_t B;
+  int64_t C;
+  int64_t ld;
+  float scale;           // gradient scale (1/B for "mean")
+  float* grad;           // kOutGrad: [B, ld]
+  uint8_t* mask;         // kOutMask: [B, C]
+  float* cand_val;       // kOutCand: [B, C]
+  int32_t* cand_idx;     // kOutCand: [B, C]
+  int32_t* cand_count;   // kOutCand: [B]
+  float* H;              // [B] or null
+  float* loss;           // [B] or null
+  int32_t* kappa;        // [B] or null
+  int32_t* status;       // device word or null
+  int mask_vec;          // mask rows are 4-byte aligned (C % 4 == 0)
+};
+
+// max() that returns NaN when either input is NaN (fmaxf would drop it).
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// Order-preserving fp32 -> uint32 key.  -0.0 is folded onto +0.0 first, so
+// that keys order exactly like the float comparison used for selection
+// (the reference keys -0.0 below +0.0, src/cuda/fw_radix_argmax.cu:60-69).
+__device__ __forceinline__ uint32_t sort_key(float z) {
+  uint32_t b = __float_as_uint(z);
+  b = (b == 0x80000000u) ? 0u : b;
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// Inverse of sort_key (maps the +0.0 key back to +0.0).
+__device__ __forceinline__ float key_value(uint32_t k) {
+  const uint32_t b = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  return __uint_as_float(b);
+}
+
+__device__ __forceinline__ float warp_max_nan(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = max_nan(v, __shfl_xor_sync(kFull, v, o));
+  return v;
+}
+
+// Butterfly sum: every lane ends with the bit-identical total (each step adds
+// a pair in both orders, which IEEE addition makes equal), and the order is
+// fixed, so the result is deterministic.
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  return v;
+}
+
+__device__ __forceinline__ int warp_sum(int v) { return __reduce_add_sync(kFull, v); }
+
+__device__ __forceinline__ int warp_excl_scan(int v, int lane) {
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(kFull, x, o);
+    if (lane >= o) x += t;
+  }
+  return x - v;
+}
+
+__device__ __forceinline__ unsigned lanemask_lt(int lane) { return (1u << lane) - 1u; }
+
+// Exact threshold on a candidate list (Michelot's fixed-point iteration,
+// i.e. Newton's method from below on f(t) = sum_j max(d_j - t, 0) - 1).
+// `L` holds n >= 1 candidate logits (a superset of the support; it always
+// contains the row maximum).  Iterates T <- {d in T : d > tau_T},
+// tau_T = (sum_T d - 1)/|T| until |T| stops changing.  The sets are nested
+// and each step removes at least one element, so at most n + 1 passes run.
+// At the fixed point every d in T is > tau_T and every removed d is <= tau_T,
+// hence T is exactly the support and tau_T = h* - M.  All lanes of the warp
+// must call it; all return the same (tau, kappa).
+__device__ __forceinline__ void michelot_list(const float* L, int n, double Md,
+                                              int lane, double& tau,
+                                              int& kappa) {
+  double t = -CUDART_INF;
+  int prev = -1;
+  for (int it = 0; it <= n; ++it) {
+    double s = 0.0;
+    int c = 0;
+    for (int i = lane; i < n; i += 32) {
+      const double d = (double)L[i] - Md;
+      if (d > t) { s += d; ++c; }
+    }
+    c = warp_sum(c);
+    s = warp_sum(s);
+    if (c == prev) break;
+    prev = c;
+    t = (s - 1.0) / (double)c;
+  }
+  tau = t;
+  kappa = prev;
+}
+
+// fp32 outputs of a solved row.  H rounds M + tau toward -inf in two directed
+// steps, so for every fp32 x: x > H <=> x > M + tau (exact real).
+__device__ __forceinline__ float threshold_fp32(float M, double tau) {
+  return __double2float_rd(__dadd_rd((double)M, tau));
+}
+
+__device__ __forceinline__ float row_loss(float M, double tau, float zy) {
+  return (float)(1.0 + ((double)M - (double)zy) + tau);
+}
+
+__device__ __forceinline__ void raise_status(int32_t* status, int bits) {
+  if (status) atomicOr(reinterpret_cast<int*>(status), bits);
+}
+
+// Streaming 128-bit load that does not pollute L1.
+__device__ __forceinline__ float4 ld_stream4(const float* p) {
+  float4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ float ld_stream1(const float* p) {
+  float r;
+  asm volatile("ld.global.nc.L1::no_allocate.f32 %0, [%1];" : "=f"(r) : "l"(p));
+  return r;
+}
+
+}  // namespace fwb200

@@ -1,0 +1,605 @@
+// Streaming tier: one CTA (CS == 1) or one thread-block cluster of CS CTAs
+// per row, for rows too long for registers (C > 2048, up to vocab scale).
+//
+// The gradient of a row is zero except on the support (kappa entries) and
+// at the label, and the support lies inside {z > M - 1}.  So the row never
+// has to be held on chip:
+//
+//   stream   every CTA streams its segment of the row once with 128-bit
+//            loads, writes the zero gradient (or zero mask) for it in the
+//            same loop, keeps a NaN-propagating running max per warp (shared
+//            across the CTA's warps through one shared-memory atomicMax) and
+//            appends elements above (running max - 1) to a per-warp
+//            candidate list (ballot compaction; when a list fills up it is
+//            re-filtered against the newer, higher threshold);
+//   exchange the CTAs publish max and list sizes; after one cluster barrier
+//            every CTA knows the row max M;
+//   solve    CTA 0 gathers the candidates z > t0 of all CTAs through DSMEM
+//            into one list, in a fixed order, and one warp runs Michelot's
+//            fixed point on it (exact support, deterministic sums);
+//   patch    CTA 0 writes the kappa support entries and the label entry over
+//            the zeros.  The zero stores of every CTA happen before the
+//            cluster barrier (release) and the patch after it (acquire), so
+//            the patch wins.
+//
+// HBM traffic is the minimum: 4C bytes read + 4C bytes written per row
+// (1 byte written for the mask; none for the candidate form).
+//
+// Dense rows (a candidate list overflowed: most of the row is within 1 of
+// the max, e.g. logits with sigma 1e-3) switch to an exact radix select over
+// order-preserving uint32 keys with 8-bit digits: per pass every CTA builds
+// a 256-bin histogram (count, fp64 sum of shifted logits) of the elements
+// above t0 inside the current key prefix, CTA 0 merges the CS histograms
+// through DSMEM, walks the bins from the top (accept / refine / stop) and
+// broadcasts the decision; at most four passes.  The row is then re-read and
+// the output rewritten densely.
+//
+// Reference counterpart: fw_precompact_histogram_kernel,
+// fw_precompact_reduce_kernel, fw_compact_multiblock_kernel,
+// fw_radix_buffer_kernel and fw_backward_candidate_kernel
+// (src/cuda/fw_radix_argmax.cu:303-429, :497-636, :638-760, :871-1035,
+// :1498-1534): five launches, two full reads of the row, an [N,K] candidate
+// buffer pair and a full memset.
+#pragma once
+
+#include <climits>
+#include <cooperative_groups.h>
+
+#include "fw_device.cuh"
+
+namespace fwb200 {
+
+constexpr int kST = 256;              // threads per CTA
+constexpr int kSW = kST / 32;         // warps per CTA
+constexpr int kStreamListCap = 128;   // candidates per warp list
+constexpr int kSolveCap = 1024;       // gathered candidates per row
+constexpr int kStreamU = 4;           // 16-byte items per thread per step
+
+struct __align__(16) StreamShared {
+  float lz[kSW][kStreamListCap];
+  int li[kSW][kStreamListCap];
+  float sz[kSolveCap];
+  int si[kSolveCap];
+  double hs[256];
+  int hc[256];
+  float wmax[kSW];
+  int wcnt[kSW];
+  unsigned run_key;
+  int flags;        // bit 0: a warp list overflowed
+  float cta_max;
+  int go_dense;     // written by CTA 0 after the gather
+  int first_idx;
+  int cand_pos;
+  float row_max;
+  int row_flags;    // bit-or of every CTA's flags
+  int nsolve;
+  // dense-path decision, written by CTA 0 into every CTA of the cluster
+  unsigned long long dec_cut;
+  double dec_sum;
+  uint32_t dec_prefix, dec_mask;
+  int dec_cnt, dec_done;
+};
+
+template <int CS>
+__device__ __forceinline__ StreamShared* cta_smem(StreamShared* s, int rank) {
+  if constexpr (CS > 1) {
+    return cooperative_groups::this_cluster().map_shared_rank(s, rank);
+  } else {
+    (void)rank;
+    return s;
+  }
+}
+
+template <int CS>
+__device__ __forceinline__ void row_barrier() {
+  if constexpr (CS > 1) {
+    cooperative_groups::this_cluster().sync();
+  } else {
+    __syncthreads();
+  }
+}
+
+// Keeps the entries > t of a warp list, in order.  Warp-collective.
+__device__ __forceinline__ int list_compact(float* lz, int* li, int cnt, float t,
+                                            int lane) {
+  constexpr int PER = kStreamListCap / 32;
+  __syncwarp();
+  float vv[PER];
+  int ii[PER];
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int e = k * 32 + lane;
+    vv[k] = (e < cnt) ? lz[e] : -CUDART_INF_F;
+    ii[k] = (e < cnt) ? li[e] : 0;
+  }
+  __syncwarp();
+  int n = 0;
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const bool keep = vv[k] > t;
+    const unsigned b = __ballot_sync(kFull, keep);
+    if (keep) {
+      const int pos = n + __popc(b & lanemask_lt(lane));
+      lz[pos] = vv[k];
+      li[pos] = ii[k];
+    }
+    n += __popc(b);
+  }
+  __syncwarp();
+  return n;
+}
+
+// Appends (val, col) for lanes with pred to the warp list.  Warp-collective;
+// cnt and ovf are warp-uniform.
+__device__ __forceinline__ void list_append(float* lz, int* li, int& cnt,
+                                            bool& ovf, float val, int col,
+                                            bool pred, float t, int lane) {
+  const unsigned b = __ballot_sync(kFull, pred);
+  if (b == 0u || ovf) return;
+  const int k = __popc(b);
+  if (cnt + k > kStreamListCap) {
+    cnt = list_compact(lz, li, cnt, t, lane);
+    if (cnt + k > kStreamListCap) {
+      ovf = true;
+      return;
+    }
+  }
+  if (pred) {
+    const int pos = cnt + __popc(b & lanemask_lt(lane));
+    lz[pos] = val;
+    li[pos] = col;
+  }
+  cnt += k;
+}
+
+// Segment of the row owned by one CTA: items [i0, i1) where an item is a
+// float4 (VEC) or a float.  With VEC, the C % 4 tail columns belong to the
+// last CTA and are handled by its warp 0.
+struct Segment {
+  int64_t i0, i1;
+};
+
+template <int CS, bool VEC>
+__device__ __forceinline__ Segment row_segment(int64_t C, int rank) {
+  const int64_t n = VEC ? C / 4 : C;
+  Segment g;
+  g.i0 = n * rank / CS;
+  g.i1 = n * (rank + 1) / CS;
+  return g;
+}
+
+// Calls f(value, column) for every element of this thread's share of the
+// segment, in the fixed order used by all passes (loads are issued kStreamU
+// 16-byte items ahead).  f must be thread-local work only.
+template <int CS, bool VEC, class F>
+__device__ __forceinline__ void for_each_element(const float* zr, int64_t C,
+                                                 int rank, F&& f) {
+  const Segment g = row_segment<CS, VEC>(C, rank);
+  constexpr int W = VEC ? 4 : 1;
+  constexpr int IPT = VEC ? kStreamU : kStreamU * 4;
+  for (int64_t base = g.i0; base < g.i1; base += (int64_t)kST * IPT) {
+    float v[IPT * W];
+#pragma unroll
+    for (int u = 0; u < IPT; ++u) {
+      const int64_t it = base + (int64_t)u * kST + threadIdx.x;
+      if (VEC) {
+        float4 q = make_float4(-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F);
+        if (it < g.i1) q = ld_stream4(zr + 4 * it);
+        v[4 * u + 0] = q.x;
+        v[4 * u + 1] = q.y;
+        v[4 * u + 2] = q.z;
+        v[4 * u + 3] = q.w;
+      } else {
+        v[u] = (it < g.i1) ? ld_stream1(zr + it) : -CUDART_INF_F;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < IPT; ++u) {
+      const int64_t it = base + (int64_t)u * kST + threadIdx.x;
+      if (it < g.i1) {
+#pragma unroll
+        for (int j = 0; j < W; ++j) f(v[u * W + j], (int)(it * W + j));
+      }
+    }
+  }
+  if (VEC && rank == CS - 1 && threadIdx.x < 32) {
+    const int64_t c = 4 * (C / 4) + threadIdx.x;
+    if (c < C) f(zr[c], (int)c);
+  }
+}
+
+template <int CS, bool VEC, int OUT>
+__global__ void __launch_bounds__(kST)
+    fw_stream_rows_kernel(RowArgs a) {
+  __shared__ StreamShared s;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int w = tid >> 5;
+  const int64_t row = blockIdx.x / CS;
+  int rank = 0;
+  if constexpr (CS > 1) rank = (int)cooperative_groups::this_cluster().block_rank();
+  const bool leader = (rank == 0);
+  const int64_t C = a.C;
+  const float* zr = a.z + row * a.ld;
+
+  if (tid == 0) {
+    s.run_key = 0u;
+    s.flags = 0;
+    s.go_dense = 0;
+    s.first_idx = INT_MAX;
+    s.cand_pos = 0;
+  }
+  __syncthreads();
+
+  // ---------------------------------------------------------------- stream
+  constexpr int W = VEC ? 4 : 1;
+  constexpr int IPT = VEC ? kStreamU : kStreamU * 4;
+  const Segment g = row_segment<CS, VEC>(C, rank);
+  float run = -CUDART_INF_F;
+  int wcnt = 0;
+  bool ovf = false;
+  float* lz = s.lz[w];
+  int* li = s.li[w];
+  float* gr = (OUT == kOutGrad) ? a.grad + row * a.ld : nullptr;
+  uint8_t* mr = (OUT == kOutMask) ? a.mask + row * C : nullptr;
+
+  for (int64_t base = g.i0; base < g.i1; base += (int64_t)kST * IPT) {
+    float v[IPT * W];
+#pragma unroll
+    for (int u = 0; u < IPT; ++u) {
+      const int64_t it = base + (int64_t)u * kST + tid;
+      if (VEC) {
+        float4 q = make_float4(-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F);
+        if (it < g.i1) q = ld_stream4(zr + 4 * it);
+        v[4 * u + 0] = q.x;
+        v[4 * u + 1] = q.y;
+        v[4 * u + 2] = q.z;
+        v[4 * u + 3] = q.w;
+      } else {
+        v[u] = (it < g.i1) ? ld_stream1(zr + it) : -CUDART_INF_F;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < IPT; ++u) {
+      const int64_t it = base + (int64_t)u * kST + tid;
+      if (it < g.i1) {
+        if (OUT == kOutGrad) {
+          if (VEC)
+            *reinterpret_cast<float4*>(gr + 4 * it) = make_float4(0.f, 0.f, 0.f, 0.f);
+          else
+            gr[it] = 0.0f;
+        } else if (OUT == kOutMask) {
+          if (VEC && a.mask_vec)
+            *reinterpret_cast<uchar4*>(mr + 4 * it) = make_uchar4(0, 0, 0, 0);
+          else
+#pragma unroll
+            for (int j = 0; j < W; ++j) mr[it * W + j] = 0;
+        }
+      }
+    }
+    float m = -CUDART_INF_F;
+#pragma unroll
+    for (int k = 0; k < IPT * W; ++k) m = max_nan(m, v[k]);
+    m = warp_max_nan(m);
+    run = max_nan(run, m);
+    if (lane == 0) atomicMax(&s.run_key, sort_key(run));
+    const float shared_max = key_value(*reinterpret_cast<volatile unsigned*>(&s.run_key));
+    const float t = __fsub_rd(fmaxf(run, shared_max), 1.0f);
+    bool anyc = false;
+#pragma unroll
+    for (int k = 0; k < IPT * W; ++k) anyc |= (v[k] > t);
+    if (__any_sync(kFull, anyc)) {
+#pragma unroll
+      for (int u = 0; u < IPT; ++u) {
+        const int64_t it = base + (int64_t)u * kST + tid;
+#pragma unroll
+        for (int j = 0; j < W; ++j)
+          list_append(lz, li, wcnt, ovf, v[u * W + j], (int)(it * W + j),
+                      v[u * W + j] > t, t, lane);
+      }
+    }
+  }
+  if (VEC && rank == CS - 1 && w == 0) {
+    // C % 4 tail columns.
+    const int64_t c = 4 * (C / 4) + lane;
+    const bool in = c < C;
+    const float x = in ? zr[c] : -CUDART_INF_F;
+    if (in) {
+      if (OUT == kOutGrad) gr[c] = 0.0f;
+      if (OUT == kOutMask) mr[c] = 0;
+    }
+    run = max_nan(run, warp_max_nan(x));
+    const float shared_max = key_value(*reinterpret_cast<volatile unsigned*>(&s.run_key));
+    const float t = __fsub_rd(fmaxf(run, shared_max), 1.0f);
+    list_append(lz, li, wcnt, ovf, x, (int)c, x > t, t, lane);
+  }
+
+  // -------------------------------------------------------------- exchange
+  if (lane == 0) {
+    s.wmax[w] = run;
+    s.wcnt[w] = wcnt;
+    if (ovf) atomicOr(&s.flags, 1);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float cm = -CUDART_INF_F;
+#pragma unroll
+    for (int k = 0; k < kSW; ++k) cm = max_nan(cm, s.wmax[k]);
+    s.cta_max = cm;
+  }
+  row_barrier<CS>();
+  if (tid == 0) {
+    float M = -CUDART_INF_F;
+    int flags = 0;
+    for (int r = 0; r < CS; ++r) {
+      const StreamShared* rs = cta_smem<CS>(&s, r);
+      M = max_nan(M, rs->cta_max);
+      flags |= rs->flags;
+    }
+    s.row_max = M;
+    s.row_flags = flags;
+  }
+  __syncthreads();
+  const float M = s.row_max;
+  const double Md = (double)M;
+  const float t0 = __fsub_rd(M, 1.0f);
+  const int64_t ylab = a.y[row];
+  const bool yok = (ylab >= 0 && ylab < C);
+  const int yc = yok ? (int)ylab : -1;
+
+  // ------------------------------------------------------- non-finite rows
+  if (!isfinite(M)) {
+    const bool isn = (M != M);
+    int best = INT_MAX;
+    for_each_element<CS, VEC>(zr, C, rank, [&](float x, int c) {
+      if (isn ? (x != x) : (x == M)) best = min(best, c);
+    });
+    best = (int)__reduce_min_sync(kFull, (unsigned)best);
+    if (lane == 0) atomicMin(&s.first_idx, best);
+    row_barrier<CS>();
+    if (leader && tid == 0) {
+      int j = INT_MAX;
+      for (int r = 0; r < CS; ++r) j = min(j, cta_smem<CS>(&s, r)->first_idx);
+      s.nsolve = j;
+    }
+    row_barrier<CS>();
+    if (!(leader && tid == 0)) return;
+    const int j = s.nsolve;
+    const float zy = yok ? zr[yc] : CUDART_NAN_F;
+    if (OUT == kOutGrad) {
+      gr[j] = a.scale - ((j == yc) ? a.scale : 0.0f);
+      if (yok && j != yc) gr[yc] = -a.scale;
+    } else if (OUT == kOutMask) {
+      mr[j] = 1;
+    } else {
+      a.cand_val[row * C] = zr[j];
+      a.cand_idx[row * C] = j;
+      if (a.cand_count) a.cand_count[row] = 1;
+    }
+    if (a.H) a.H[row] = M;
+    if (a.loss) a.loss[row] = yok ? (1.0f - zy + M) : CUDART_NAN_F;
+    if (a.kappa) a.kappa[row] = 1;
+    if (!yok) raise_status(a.status, 1);
+    raise_status(a.status, 2);
+    return;
+  }
+
+  // ---------------------------------------------------------------- gather
+  if (!(s.row_flags & 1) && leader && w == 0) {
+    int n = 0;
+    bool full = false;
+    for (int r = 0; r < CS && !full; ++r) {
+      const StreamShared* rs = cta_smem<CS>(&s, r);
+      for (int ww = 0; ww < kSW && !full; ++ww) {
+        const int cnt = rs->wcnt[ww];
+        for (int k0 = 0; k0 < cnt; k0 += 32) {
+          const int k = k0 + lane;
+          float val = -CUDART_INF_F;
+          int col = 0;
+          if (k < cnt) {
+            val = rs->lz[ww][k];
+            col = rs->li[ww][k];
+          }
+          const bool keep = val > t0;
+          const unsigned b = __ballot_sync(kFull, keep);
+          if (n + __popc(b) > kSolveCap) {
+            full = true;
+            break;
+          }
+          if (keep) {
+            const int pos = n + __popc(b & lanemask_lt(lane));
+            s.sz[pos] = val;
+            s.si[pos] = col;
+          }
+          n += __popc(b);
+        }
+      }
+    }
+    if (lane == 0) {
+      s.nsolve = n;
+      for (int r = 0; r < CS; ++r) cta_smem<CS>(&s, r)->go_dense = full ? 1 : 0;
+    }
+  }
+  row_barrier<CS>();
+  const bool dense = (s.row_flags & 1) || s.go_dense;
+
+  // ------------------------------------------------------ solve and patch
+  if (!dense) {
+    if (!(leader && w == 0)) return;
+    const int n = s.nsolve;
+    double tau;
+    int kap;
+    michelot_list(s.sz, n, Md, lane, tau, kap);
+    if (OUT == kOutGrad) {
+      const float inv = (float)((double)a.scale / (double)kap);
+      bool ysel = false;
+      for (int k = lane; k < n; k += 32) {
+        const int col = s.si[k];
+        if ((double)s.sz[k] - Md > tau) {
+          float gv = inv;
+          if (col == yc) {
+            gv -= a.scale;
+            ysel = true;
+          }
+          gr[col] = gv;
+        }
+      }
+      ysel = __any_sync(kFull, ysel);
+      if (lane == 0 && yok && !ysel) gr[yc] = -a.scale;
+    } else if (OUT == kOutMask) {
+      for (int k = lane; k < n; k += 32)
+        if ((double)s.sz[k] - Md > tau) mr[s.si[k]] = 1;
+    } else {
+      float* cv = a.cand_val + row * C;
+      int32_t* ci = a.cand_idx + row * C;
+      int pos0 = 0;
+      for (int k0 = 0; k0 < n; k0 += 32) {
+        const int k = k0 + lane;
+        const bool sel = (k < n) && ((double)s.sz[k] - Md > tau);
+        const unsigned b = __ballot_sync(kFull, sel);
+        if (sel) {
+          const int pos = pos0 + __popc(b & lanemask_lt(lane));
+          cv[pos] = s.sz[k];
+          ci[pos] = s.si[k];
+        }
+        pos0 += __popc(b);
+      }
+      if (lane == 0 && a.cand_count) a.cand_count[row] = kap;
+    }
+    if (lane == 0) {
+      const float zy = yok ? zr[yc] : CUDART_NAN_F;
+      if (a.H) a.H[row] = threshold_fp32(M, tau);
+      if (a.loss) a.loss[row] = yok ? row_loss(M, tau, zy) : CUDART_NAN_F;
+      if (a.kappa) a.kappa[row] = kap;
+      if (!yok) raise_status(a.status, 1);
+    }
+    return;
+  }
+
+  // ------------------------------------------------ dense rows: radix select
+  uint32_t prefix = 0u, pmask = 0u;
+  int cnt_a = 0;
+  double sum_a = 0.0;
+  unsigned long long cut = 1ull << 32;  // selected <=> key >= cut (and z > t0)
+  const double t0d = (double)t0 - Md;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int b = tid; b < 256; b += kST) {
+      s.hc[b] = 0;
+      s.hs[b] = 0.0;
+    }
+    __syncthreads();
+    for_each_element<CS, VEC>(zr, C, rank, [&](float x, int) {
+      if (x > t0) {
+        const uint32_t k = sort_key(x);
+        if ((k & pmask) == prefix) {
+          const int bin = (int)((k >> shift) & 255u);
+          atomicAdd(&s.hc[bin], 1);
+          atomicAdd(&s.hs[bin], (double)x - Md);
+        }
+      }
+    });
+    row_barrier<CS>();
+    if (leader) {
+      if (CS > 1) {
+        for (int b = tid; b < 256; b += kST) {
+          int c = s.hc[b];
+          double sm = s.hs[b];
+          for (int r = 1; r < CS; ++r) {
+            const StreamShared* rs = cta_smem<CS>(&s, r);
+            c += rs->hc[b];
+            sm += rs->hs[b];
+          }
+          s.hc[b] = c;
+          s.hs[b] = sm;
+        }
+        __syncthreads();
+      }
+      if (tid == 0) {
+        bool refine = false, done = false;
+        for (int b = 255; b >= 0; --b) {
+          const int cb = s.hc[b];
+          if (cb == 0) continue;
+          const double sb = s.hs[b];
+          const uint32_t lo_key = prefix | ((uint32_t)b << shift);
+          const uint32_t hi_key = lo_key | ((1u << shift) - 1u);
+          double lo = (double)key_value(lo_key) - Md;
+          double hi = (double)key_value(hi_key) - Md;
+          if (lo != lo) lo = -CUDART_INF;
+          if (hi != hi) hi = CUDART_INF;
+          const double lo_eff = fmax(lo, t0d);
+          // f(t) = sum_{d > t} (d - t): every element of this bin and above
+          // is >= lo_eff, so f(min of bin) <= f(lo_eff).
+          if ((sum_a + sb) - (double)(cnt_a + cb) * lo_eff < 1.0) {
+            cnt_a += cb;
+            sum_a += sb;
+            cut = lo_key;
+            continue;
+          }
+          // Nothing in this bin exceeds hi, so f(max of bin) >= f(hi).
+          if (cnt_a > 0 && sum_a - (double)cnt_a * hi >= 1.0) {
+            done = true;
+            break;
+          }
+          prefix = lo_key;
+          pmask |= 0xffu << shift;
+          refine = true;
+          break;
+        }
+        if (!refine) done = true;
+        for (int r = 0; r < CS; ++r) {
+          StreamShared* rs = cta_smem<CS>(&s, r);
+          rs->dec_prefix = prefix;
+          rs->dec_mask = pmask;
+          rs->dec_cnt = cnt_a;
+          rs->dec_sum = sum_a;
+          rs->dec_cut = cut;
+          rs->dec_done = done ? 1 : 0;
+        }
+      }
+    }
+    row_barrier<CS>();
+    prefix = s.dec_prefix;
+    pmask = s.dec_mask;
+    cnt_a = s.dec_cnt;
+    sum_a = s.dec_sum;
+    cut = s.dec_cut;
+    if (s.dec_done) break;
+  }
+  const int kap = cnt_a;
+  const double tau = (sum_a - 1.0) / (double)kap;
+  const float inv = (float)((double)a.scale / (double)kap);
+  auto sel_of = [&](float x) -> bool {
+    return x > t0 && (unsigned long long)sort_key(x) >= cut;
+  };
+  if (OUT == kOutGrad) {
+    for_each_element<CS, VEC>(zr, C, rank, [&](float x, int c) {
+      float gv = sel_of(x) ? inv : 0.0f;
+      if (c == yc) gv -= a.scale;
+      gr[c] = gv;
+    });
+  } else if (OUT == kOutMask) {
+    for_each_element<CS, VEC>(zr, C, rank, [&](float x, int c) { mr[c] = sel_of(x) ? 1 : 0; });
+  } else {
+    int* pos_ctr = &cta_smem<CS>(&s, 0)->cand_pos;
+    float* cv = a.cand_val + row * C;
+    int32_t* ci = a.cand_idx + row * C;
+    for_each_element<CS, VEC>(zr, C, rank, [&](float x, int c) {
+      if (sel_of(x)) {
+        const int p = atomicAdd(pos_ctr, 1);
+        cv[p] = x;
+        ci[p] = c;
+      }
+    });
+  }
+  row_barrier<CS>();
+  if (leader && tid == 0) {
+    const float zy = yok ? zr[yc] : CUDART_NAN_F;
+    if (a.H) a.H[row] = threshold_fp32(M, tau);
+    if (a.loss) a.loss[row] = yok ? row_loss(M, tau, zy) : CUDART_NAN_F;
+    if (a.kappa) a.kappa[row] = kap;
+    if (OUT == kOutCand && a.cand_count) a.cand_count[row] = kap;
+    if (!yok) raise_status(a.status, 1);
+  }
+}
+
+}  // namespace fwb200

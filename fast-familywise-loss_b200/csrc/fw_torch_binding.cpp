@@ -1,0 +1,241 @@
+// Python module `fw_radix_cuda`: drop-in for the reference's pybind11 module
+// of the same name (src/cuda/binding.cpp:1-13), built on the C ABI of
+// libfwloss_b200.so (include/fwloss_b200.h).
+//
+// The four reference functions keep their names, arguments, output tuples,
+// dtypes (H/losses/mean fp32, kappa int32, selected bool, candidates
+// fp32/int32) and the hard-coded "mean" scaling of the gradient (1/N).
+// Differences, all in the direction of stricter checking:
+//   * launches go to the current torch stream of the logits' device (under a
+//     device guard) instead of the legacy default stream;
+//   * targets are checked (1-D int64, N entries, same device); logits may be
+//     non-contiguous along rows (row stride is passed through);
+//   * `mean` is a fixed-order fp64 reduction (deterministic);
+//   * candidate_buffer/indices rows hold exactly the support (kappa entries),
+//     so fw_backward needs no zero-initialised [N,K] buffer.
+// Extra functions used by the autograd layer (fwloss_b200 package):
+//   fused_fwd_bwd, scale_grad, loss_reduce.
+#include <torch/extension.h>
+
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <vector>
+
+#include "../../include/fwloss_b200.h"
+
+namespace {
+
+void check_rc(int rc, const char* what) {
+  TORCH_CHECK(rc == FWB_OK, what, " failed: ", fw_error_string(rc));
+}
+
+void check_logits(const torch::Tensor& logits) {
+  TORCH_CHECK(logits.is_cuda(), "logits must be a CUDA tensor");
+  TORCH_CHECK(logits.dim() == 2, "logits must have shape [N, K]");
+  TORCH_CHECK(logits.scalar_type() == torch::kFloat32, "logits must be float32");
+  TORCH_CHECK(logits.size(1) >= 1, "logits must have K >= 1 columns");
+}
+
+void check_targets(const torch::Tensor& targets, int64_t N, const torch::Tensor& like) {
+  TORCH_CHECK(targets.is_cuda() && targets.device() == like.device(),
+              "targets must be a CUDA tensor on the logits' device");
+  TORCH_CHECK(targets.dim() == 1 && targets.size(0) == N, "targets must have shape [N]");
+  TORCH_CHECK(targets.scalar_type() == torch::kLong, "targets must be int64");
+}
+
+// Row-major view with unit column stride; returns the row stride.
+torch::Tensor rows_view(const torch::Tensor& logits, int64_t* ld) {
+  torch::Tensor z = logits;
+  if (z.stride(1) != 1 || z.stride(0) < z.size(1)) z = z.contiguous();
+  *ld = z.size(0) > 1 ? z.stride(0) : z.size(1);
+  if (*ld < z.size(1)) *ld = z.size(1);
+  return z;
+}
+
+void* cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+torch::Tensor mean_of(const torch::Tensor& losses) {
+  auto out = torch::empty({}, losses.options());
+  const int64_t n = losses.size(0);
+  check_rc(fw_loss_reduce(losses.data_ptr<float>(), n, n > 0 ? 1.0 / (double)n : NAN,
+                          out.data_ptr<float>(), cur_stream()),
+           "fw_loss_reduce");
+  return out;
+}
+
+torch::TensorOptions i32(const torch::Tensor& like) {
+  return torch::TensorOptions().dtype(torch::kInt32).device(like.device());
+}
+
+}  // namespace
+
+// reference: fw_radix_forward_small (src/cuda/fw_radix_argmax.cu:1381-1414)
+std::vector<torch::Tensor> fw_forward_small(torch::Tensor logits, torch::Tensor targets) {
+  check_logits(logits);
+  const c10::cuda::CUDAGuard guard(logits.device());
+  const int64_t N = logits.size(0), K = logits.size(1);
+  check_targets(targets, N, logits);
+  int64_t ld = K;
+  auto z = rows_view(logits, &ld);
+  auto y = targets.contiguous();
+  auto selected = torch::empty({N, K}, logits.options().dtype(torch::kBool));
+  auto H = torch::empty({N}, logits.options());
+  auto losses = torch::empty({N}, logits.options());
+  auto kappa = torch::empty({N}, i32(logits));
+  check_rc(fw_forward_mask(z.data_ptr<float>(), y.data_ptr<int64_t>(), N, K, ld,
+                           H.data_ptr<float>(), losses.data_ptr<float>(), kappa.data_ptr<int32_t>(),
+                           reinterpret_cast<uint8_t*>(selected.data_ptr<bool>()), nullptr,
+                           cur_stream()),
+           "fw_forward_mask");
+  return {H, losses, mean_of(losses), kappa, selected};
+}
+
+// reference: fw_radix_backward_small (src/cuda/fw_radix_argmax.cu:1591-1608)
+torch::Tensor fw_backward_small(torch::Tensor targets, torch::Tensor selected_logits,
+                                torch::Tensor kappas) {
+  TORCH_CHECK(selected_logits.is_cuda() && selected_logits.dim() == 2 &&
+                  selected_logits.scalar_type() == torch::kBool,
+              "selected_logits must be a 2-D CUDA bool tensor");
+  const c10::cuda::CUDAGuard guard(selected_logits.device());
+  const int64_t N = selected_logits.size(0), K = selected_logits.size(1);
+  check_targets(targets, N, selected_logits);
+  TORCH_CHECK(kappas.is_cuda() && kappas.numel() == N && kappas.scalar_type() == torch::kInt32,
+              "kappas must be an int32 CUDA tensor with N entries");
+  auto sel = selected_logits.contiguous();
+  auto y = targets.contiguous();
+  auto kap = kappas.contiguous();
+  auto grad = torch::empty({N, K}, selected_logits.options().dtype(torch::kFloat32));
+  check_rc(fw_backward_mask(y.data_ptr<int64_t>(), reinterpret_cast<const uint8_t*>(sel.data_ptr<bool>()),
+                            kap.data_ptr<int32_t>(), N, K, N > 0 ? 1.0f / (float)N : 0.0f,
+                            grad.data_ptr<float>(), nullptr, cur_stream()),
+           "fw_backward_mask");
+  return grad;
+}
+
+// reference: fw_radix_forward (src/cuda/fw_radix_argmax.cu:1417-1496)
+std::vector<torch::Tensor> fw_forward(torch::Tensor logits, torch::Tensor targets) {
+  check_logits(logits);
+  const c10::cuda::CUDAGuard guard(logits.device());
+  const int64_t N = logits.size(0), K = logits.size(1);
+  check_targets(targets, N, logits);
+  int64_t ld = K;
+  auto z = rows_view(logits, &ld);
+  auto y = targets.contiguous();
+  auto cand_val = torch::empty({N, K}, logits.options());
+  auto cand_idx = torch::empty({N, K}, i32(logits));
+  auto cand_cnt = torch::empty({N}, i32(logits));
+  auto H = torch::empty({N}, logits.options());
+  auto losses = torch::empty({N}, logits.options());
+  auto kappa = torch::empty({N}, i32(logits));
+  check_rc(fw_forward_candidates(z.data_ptr<float>(), y.data_ptr<int64_t>(), N, K, ld,
+                                 H.data_ptr<float>(), losses.data_ptr<float>(),
+                                 kappa.data_ptr<int32_t>(), cand_val.data_ptr<float>(),
+                                 cand_idx.data_ptr<int32_t>(), cand_cnt.data_ptr<int32_t>(), nullptr,
+                                 cur_stream()),
+           "fw_forward_candidates");
+  return {H, losses, mean_of(losses), kappa, cand_val, cand_idx, cand_cnt};
+}
+
+// reference: fw_radix_backward (src/cuda/fw_radix_argmax.cu:1536-1559)
+torch::Tensor fw_backward(torch::Tensor logits, torch::Tensor targets, torch::Tensor H,
+                          torch::Tensor kappas, torch::Tensor candidate_buffer,
+                          torch::Tensor candidate_indices, torch::Tensor candidate_counts) {
+  check_logits(logits);
+  const c10::cuda::CUDAGuard guard(logits.device());
+  const int64_t N = logits.size(0), K = logits.size(1);
+  check_targets(targets, N, logits);
+  TORCH_CHECK(H.is_cuda() && H.numel() == N && H.scalar_type() == torch::kFloat32, "H must be float32 [N]");
+  TORCH_CHECK(kappas.is_cuda() && kappas.numel() == N && kappas.scalar_type() == torch::kInt32,
+              "kappas must be int32 [N]");
+  TORCH_CHECK(candidate_buffer.is_cuda() && candidate_buffer.numel() == N * K &&
+                  candidate_buffer.scalar_type() == torch::kFloat32,
+              "candidate_buffer must be float32 [N, K]");
+  TORCH_CHECK(candidate_indices.is_cuda() && candidate_indices.numel() == N * K &&
+                  candidate_indices.scalar_type() == torch::kInt32,
+              "candidate_indices must be int32 [N, K]");
+  TORCH_CHECK(candidate_counts.is_cuda() && candidate_counts.numel() == N &&
+                  candidate_counts.scalar_type() == torch::kInt32,
+              "candidate_counts must be int32 [N]");
+  auto y = targets.contiguous();
+  auto cv = candidate_buffer.contiguous();
+  auto ci = candidate_indices.contiguous();
+  auto cc = candidate_counts.contiguous();
+  auto h = H.contiguous();
+  auto kap = kappas.contiguous();
+  auto grad = torch::empty({N, K}, logits.options());
+  check_rc(fw_backward_candidates(cv.data_ptr<float>(), ci.data_ptr<int32_t>(), cc.data_ptr<int32_t>(),
+                                  h.data_ptr<float>(), kap.data_ptr<int32_t>(), y.data_ptr<int64_t>(),
+                                  N, K, N > 0 ? 1.0f / (float)N : 0.0f, grad.data_ptr<float>(),
+                                  nullptr, cur_stream()),
+           "fw_backward_candidates");
+  return grad;
+}
+
+// Fused forward + backward (new): (grad, H, losses, kappa), grad scaled by
+// grad_scale; `status` is an optional int32 [1] device word.
+std::vector<torch::Tensor> fused_fwd_bwd(torch::Tensor logits, torch::Tensor targets,
+                                         double grad_scale, c10::optional<torch::Tensor> status) {
+  check_logits(logits);
+  const c10::cuda::CUDAGuard guard(logits.device());
+  const int64_t N = logits.size(0), K = logits.size(1);
+  check_targets(targets, N, logits);
+  int64_t ld = K;
+  auto z = rows_view(logits, &ld);
+  auto y = targets.contiguous();
+  auto grad = (ld == K) ? torch::empty({N, K}, logits.options())
+                        : torch::empty_strided({N, K}, {ld, 1}, logits.options());
+  auto H = torch::empty({N}, logits.options());
+  auto losses = torch::empty({N}, logits.options());
+  auto kappa = torch::empty({N}, i32(logits));
+  int32_t* st = nullptr;
+  if (status.has_value()) {
+    TORCH_CHECK(status->is_cuda() && status->scalar_type() == torch::kInt32 && status->numel() >= 1,
+                "status must be an int32 CUDA tensor");
+    st = status->data_ptr<int32_t>();
+  }
+  check_rc(fw_fused_fwd_bwd(z.data_ptr<float>(), y.data_ptr<int64_t>(), N, K, ld, (float)grad_scale,
+                            grad.data_ptr<float>(), H.data_ptr<float>(), losses.data_ptr<float>(),
+                            kappa.data_ptr<int32_t>(), st, cur_stream()),
+           "fw_fused_fwd_bwd");
+  return {grad, H, losses, kappa};
+}
+
+// grad (in place) *= grad_output[per_row ? r : 0] / assumed_scale.
+void scale_grad(torch::Tensor grad, torch::Tensor grad_output, bool per_row, double assumed_scale) {
+  TORCH_CHECK(grad.is_cuda() && grad.dim() == 2 && grad.scalar_type() == torch::kFloat32 &&
+                  grad.stride(1) == 1,
+              "grad must be a row-major float32 CUDA matrix");
+  const c10::cuda::CUDAGuard guard(grad.device());
+  auto go = grad_output.to(grad.device(), torch::kFloat32).contiguous();
+  TORCH_CHECK(go.numel() >= (per_row ? grad.size(0) : 1), "grad_output too small");
+  const int64_t ld = grad.size(0) > 1 ? grad.stride(0) : grad.size(1);
+  check_rc(fw_scale_grad(grad.data_ptr<float>(), go.data_ptr<float>(), per_row ? 1 : 0,
+                         (float)assumed_scale, grad.size(0), grad.size(1), ld, cur_stream()),
+           "fw_scale_grad");
+}
+
+// scale * sum(losses), fixed-order fp64 reduction; 0-d float32.
+torch::Tensor loss_reduce(torch::Tensor losses, double scale) {
+  TORCH_CHECK(losses.is_cuda() && losses.scalar_type() == torch::kFloat32 && losses.dim() == 1,
+              "losses must be a float32 CUDA vector");
+  const c10::cuda::CUDAGuard guard(losses.device());
+  auto l = losses.contiguous();
+  auto out = torch::empty({}, l.options());
+  check_rc(fw_loss_reduce(l.data_ptr<float>(), l.size(0), scale, out.data_ptr<float>(), cur_stream()),
+           "fw_loss_reduce");
+  return out;
+}
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "B200 (sm_100a) Familywise loss: drop-in for the fw_radix_cuda module";
+  m.def("fw_forward", &fw_forward, "FW forward (support as candidate lists)");
+  m.def("fw_backward", &fw_backward, "FW backward from candidate lists (mean scaling)");
+  m.def("fw_forward_small", &fw_forward_small, "FW forward (support as bool mask)");
+  m.def("fw_backward_small", &fw_backward_small, "FW backward from the bool mask (mean scaling)");
+  m.def("fused_fwd_bwd", &fused_fwd_bwd, "fused forward+backward: (grad, H, losses, kappa)",
+        py::arg("logits"), py::arg("targets"), py::arg("grad_scale"), py::arg("status") = py::none());
+  m.def("scale_grad", &scale_grad, "in-place grad scaling by a device-side grad_output");
+  m.def("loss_reduce", &loss_reduce, "deterministic scale * sum(losses)");
+  m.def("version", []() { return std::string(fw_version()); });
+}

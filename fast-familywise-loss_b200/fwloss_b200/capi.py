@@ -1,0 +1,164 @@
+"""ctypes binding of the C ABI in libfwloss_b200.so (include/fwloss_b200.h).
+
+Every wrapper takes CUDA tensors, passes raw device pointers, sizes and the
+current torch stream of the tensors' device, and raises FWError on a non-zero
+return code.  Nothing here computes anything: all work happens in the CUDA
+kernels behind the C ABI.  This is the path the GPU parity tests use, and the
+template for a non-Python binding (see INTEGRATION.md at the repository root).
+"""
+import ctypes
+import os
+
+import torch
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libfwloss_b200.so")
+
+FWB_OK = 0
+FWB_STATUS_LABEL_RANGE = 1
+FWB_STATUS_NONFINITE = 2
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_SIGS = {
+    "fw_version": ([], ctypes.c_char_p),
+    "fw_error_string": ([ctypes.c_int], ctypes.c_char_p),
+    "fw_fused_fwd_bwd": ([_P, _P, _I64, _I64, _I64, ctypes.c_float, _P, _P, _P, _P, _P, _P], ctypes.c_int),
+    "fw_forward_mask": ([_P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P], ctypes.c_int),
+    "fw_backward_mask": ([_P, _P, _P, _I64, _I64, ctypes.c_float, _P, _P, _P], ctypes.c_int),
+    "fw_forward_candidates": ([_P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P], ctypes.c_int),
+    "fw_backward_candidates": ([_P, _P, _P, _P, _P, _P, _I64, _I64, ctypes.c_float, _P, _P, _P], ctypes.c_int),
+    "fw_scale_grad": ([_P, _P, ctypes.c_int, ctypes.c_float, _I64, _I64, _I64, _P], ctypes.c_int),
+    "fw_loss_reduce": ([_P, _I64, ctypes.c_double, _P, _P], ctypes.c_int),
+}
+EXPORTED = tuple(_SIGS)
+
+_lib = None
+
+
+class FWError(RuntimeError):
+    pass
+
+
+def load():
+    """Loads the library (once) and declares the prototypes."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise FWError(f"{LIB_PATH} is missing: run `python build_native.py` in the package directory")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (args, res) in _SIGS.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = lib
+    return _lib
+
+
+def version():
+    return load().fw_version().decode()
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(t):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _check(rc, what):
+    if rc != FWB_OK:
+        raise FWError(f"{what}: {load().fw_error_string(rc).decode()} (code {rc})")
+
+
+def _rows(z):
+    if z.dim() != 2 or z.dtype != torch.float32 or not z.is_cuda:
+        raise FWError("logits must be a 2-D float32 CUDA tensor")
+    if z.stride(1) != 1 or (z.size(0) > 1 and z.stride(0) < z.size(1)):
+        z = z.contiguous()
+    ld = z.stride(0) if z.size(0) > 1 else z.size(1)
+    return z, max(ld, z.size(1))
+
+
+def fused_fwd_bwd(z, y, grad_scale, grad=None, status=None):
+    """(grad, H, loss, kappa) from the fused kernel; grad has z's row stride."""
+    z, ld = _rows(z)
+    B, C = z.shape
+    if grad is None:
+        grad = torch.empty_strided((B, C), (ld, 1), dtype=torch.float32, device=z.device)
+    H = torch.empty(B, dtype=torch.float32, device=z.device)
+    loss = torch.empty(B, dtype=torch.float32, device=z.device)
+    kappa = torch.empty(B, dtype=torch.int32, device=z.device)
+    lib = load()
+    with torch.cuda.device(z.device):
+        _check(lib.fw_fused_fwd_bwd(_ptr(z), _ptr(y), B, C, ld, float(grad_scale), _ptr(grad),
+                                    _ptr(H), _ptr(loss), _ptr(kappa), _ptr(status), _stream(z)),
+               "fw_fused_fwd_bwd")
+    return grad, H, loss, kappa
+
+
+def forward_mask(z, y, status=None):
+    z, ld = _rows(z)
+    B, C = z.shape
+    mask = torch.empty((B, C), dtype=torch.bool, device=z.device)
+    H = torch.empty(B, dtype=torch.float32, device=z.device)
+    loss = torch.empty(B, dtype=torch.float32, device=z.device)
+    kappa = torch.empty(B, dtype=torch.int32, device=z.device)
+    with torch.cuda.device(z.device):
+        _check(load().fw_forward_mask(_ptr(z), _ptr(y), B, C, ld, _ptr(H), _ptr(loss), _ptr(kappa),
+                                      _ptr(mask), _ptr(status), _stream(z)), "fw_forward_mask")
+    return H, loss, kappa, mask
+
+
+def backward_mask(y, mask, kappa, grad_scale, status=None):
+    B, C = mask.shape
+    grad = torch.empty((B, C), dtype=torch.float32, device=mask.device)
+    with torch.cuda.device(mask.device):
+        _check(load().fw_backward_mask(_ptr(y), _ptr(mask.contiguous()), _ptr(kappa), B, C,
+                                       float(grad_scale), _ptr(grad), _ptr(status), _stream(mask)),
+               "fw_backward_mask")
+    return grad
+
+
+def forward_candidates(z, y, status=None):
+    z, ld = _rows(z)
+    B, C = z.shape
+    dev = z.device
+    cv = torch.empty((B, C), dtype=torch.float32, device=dev)
+    ci = torch.empty((B, C), dtype=torch.int32, device=dev)
+    cc = torch.empty(B, dtype=torch.int32, device=dev)
+    H = torch.empty(B, dtype=torch.float32, device=dev)
+    loss = torch.empty(B, dtype=torch.float32, device=dev)
+    kappa = torch.empty(B, dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        _check(load().fw_forward_candidates(_ptr(z), _ptr(y), B, C, ld, _ptr(H), _ptr(loss),
+                                            _ptr(kappa), _ptr(cv), _ptr(ci), _ptr(cc), _ptr(status),
+                                            _stream(z)), "fw_forward_candidates")
+    return H, loss, kappa, cv, ci, cc
+
+
+def backward_candidates(cv, ci, cc, H, kappa, y, grad_scale, status=None):
+    B, C = cv.shape
+    grad = torch.empty((B, C), dtype=torch.float32, device=cv.device)
+    with torch.cuda.device(cv.device):
+        _check(load().fw_backward_candidates(_ptr(cv), _ptr(ci), _ptr(cc), _ptr(H), _ptr(kappa),
+                                             _ptr(y), B, C, float(grad_scale), _ptr(grad),
+                                             _ptr(status), _stream(cv)), "fw_backward_candidates")
+    return grad
+
+
+def scale_grad(grad, grad_output, per_row, assumed_scale):
+    B, C = grad.shape
+    ld = grad.stride(0) if B > 1 else C
+    with torch.cuda.device(grad.device):
+        _check(load().fw_scale_grad(_ptr(grad), _ptr(grad_output), int(bool(per_row)),
+                                    float(assumed_scale), B, C, ld, _stream(grad)), "fw_scale_grad")
+    return grad
+
+
+def loss_reduce(loss, scale):
+    out = torch.empty((), dtype=torch.float32, device=loss.device)
+    with torch.cuda.device(loss.device):
+        _check(load().fw_loss_reduce(_ptr(loss), loss.numel(), float(scale), _ptr(out),
+                                     _stream(loss)), "fw_loss_reduce")
+    return out

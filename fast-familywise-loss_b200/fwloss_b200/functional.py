@@ -1,0 +1,115 @@
+"""Autograd front-end of the fused FW-loss kernels.
+
+    from fwloss_b200 import familywise_loss
+    loss = familywise_loss(logits, target, reduction="mean")   # logits: [N, K] fp32 CUDA
+    loss.backward()
+
+Mirrors the CPU extension's `fwcpp.familywise_loss(logits, target,
+reduction)` (src/cpu/fwcpp.py:18-19, src/cpu/fw_cpu.cpp:721-749): the
+gradient is produced by the forward kernel (one read of the logits, one write
+of the gradient) and saved; backward only applies the upstream gradient.
+Unlike the CPU version, backward never synchronises with the host: the
+upstream gradient is read on the device, and rows whose factor is exactly 1
+(the usual `loss.backward()`) are left untouched.  "none" is supported in
+addition to "mean" and "sum".
+"""
+import torch
+
+from ._native import ext
+
+_REDUCTIONS = ("mean", "sum", "none")
+
+
+def _check_inputs(logits, target):
+    if not (isinstance(logits, torch.Tensor) and logits.is_cuda):
+        raise TypeError("familywise_loss: logits must be a CUDA tensor (this build has no CPU path)")
+    if logits.dim() != 2 or logits.dtype != torch.float32:
+        raise TypeError("familywise_loss: logits must be a 2-D float32 tensor [N, K]")
+    if target.dim() != 1 or target.shape[0] != logits.shape[0]:
+        raise ValueError("familywise_loss: target must have shape [N]")
+    if target.dtype != torch.int64:
+        raise TypeError("familywise_loss: target must be int64")
+    if target.device != logits.device:
+        raise ValueError("familywise_loss: target must be on the logits' device")
+
+
+class _FWRows(torch.autograd.Function):
+    """Per-row losses [N] (differentiable), H [N] and kappa [N] (not).
+
+    The gradient is computed in forward with scale `assumed`; backward
+    multiplies row r by grad_losses[r] / assumed on the device.
+    """
+
+    @staticmethod
+    def forward(ctx, logits, target, assumed, status):
+        grad, H, losses, kappa = ext().fused_fwd_bwd(logits.detach(), target, float(assumed), status)
+        ctx.grad = grad
+        ctx.assumed = float(assumed)
+        ctx.mark_non_differentiable(H, kappa)
+        return losses, H, kappa
+
+    @staticmethod
+    def backward(ctx, g_losses, g_H, g_kappa):
+        grad = ctx.grad
+        ctx.grad = None
+        if g_losses is None:
+            return None, None, None, None
+        ext().scale_grad(grad, g_losses.contiguous(), True, ctx.assumed)
+        return grad, None, None, None
+
+
+class _FWReduced(torch.autograd.Function):
+    """scale * sum of the per-row losses as a 0-d tensor ("mean"/"sum")."""
+
+    @staticmethod
+    def forward(ctx, logits, target, scale, status):
+        grad, H, losses, kappa = ext().fused_fwd_bwd(logits.detach(), target, float(scale), status)
+        ctx.grad = grad
+        return ext().loss_reduce(losses, float(scale))
+
+    @staticmethod
+    def backward(ctx, g):
+        grad = ctx.grad
+        ctx.grad = None
+        ext().scale_grad(grad, g.reshape(1), False, 1.0)
+        return grad, None, None, None
+
+
+class _MeanOfRows(torch.autograd.Function):
+    """Deterministic mean of a loss vector (fixed-order fp64 reduction)."""
+
+    @staticmethod
+    def forward(ctx, losses):
+        ctx.n = losses.shape[0]
+        return ext().loss_reduce(losses, 1.0 / ctx.n if ctx.n else float("nan"))
+
+    @staticmethod
+    def backward(ctx, g):
+        return (g * (1.0 / ctx.n)).expand(ctx.n)
+
+
+def familywise_loss(logits, target, reduction="mean", status=None):
+    """FW loss of logits [N, K] (fp32, CUDA) against int64 targets [N].
+
+    reduction "mean" / "sum" return a 0-d tensor, "none" the per-row losses.
+    `status`, if given, is an int32 CUDA tensor whose first word receives the
+    bit-or of FWB_STATUS_* flags (label out of range, non-finite row).
+    """
+    if reduction not in _REDUCTIONS:
+        raise ValueError(f"Invalid reduction mode: {reduction}")
+    _check_inputs(logits, target)
+    n = logits.shape[0]
+    if reduction == "none":
+        return _FWRows.apply(logits, target, 1.0, status)[0]
+    scale = (1.0 / n if n else float("nan")) if reduction == "mean" else 1.0
+    return _FWReduced.apply(logits, target, scale, status)
+
+
+def fw_rows(logits, target, assumed_scale=1.0, status=None):
+    """(losses [N] differentiable, H [N] fp32, kappa [N] int32)."""
+    _check_inputs(logits, target)
+    return _FWRows.apply(logits, target, float(assumed_scale), status)
+
+
+def mean_of_rows(losses):
+    return _MeanOfRows.apply(losses)

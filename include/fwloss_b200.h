@@ -1,0 +1,147 @@
+/*
+ * fwloss_b200.h -- C ABI of the B200 (sm_100a) Familywise-loss library.
+ *
+ * The Familywise (FW) loss of one row z[0..C) with label y is
+ *     L(z, y) = 1 - z_y + h*,   h* = max_k (S_k - 1) / k,
+ * S_k being the sum of the k largest logits.  h* is also the root of
+ * sum_j max(z_j - h, 0) = 1, and the gradient is
+ *     dL/dz = (1/kappa) 1[z > h*] - e_y,   kappa = |{j : z_j > h*}|.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (passed as void*, NULL = legacy default stream), launches asynchronously on
+ * that stream and returns an int status (FWB_OK or one of the FWB_E* codes
+ * below).  Nothing here allocates device memory, synchronises the stream or
+ * reads device data on the host.  Logits are fp32 row-major with row stride
+ * `ld` (elements, ld >= C); labels are int64.  Data-dependent problems that
+ * only the device can see (a label outside [0, C), a non-finite row maximum)
+ * are reported through the optional device word `status` (bit-or of
+ * FWB_STATUS_* flags; the caller zeroes it) and by a NaN loss for that row.
+ *
+ * Outputs per row r (all optional pointers may be NULL):
+ *   H[r]      fp32 threshold, rounded toward -inf from the exact h*, so that
+ *             for every fp32 x:  x > H[r]  <=>  x > h*.
+ *   loss[r]   fp32 1 - z_y + h*.
+ *   kappa[r]  int32 support size.
+ * Thresholds and kappa are computed by the same procedure in every entry
+ * point, so the mask-, candidate- and gradient-producing paths agree.
+ */
+#ifndef FWLOSS_B200_H
+#define FWLOSS_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FWB_API __attribute__((visibility("default")))
+#else
+#define FWB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FWB_OK 0
+#define FWB_E_SHAPE 1      /* B < 0, C < 1, ld < C, or a size overflows      */
+#define FWB_E_POINTER 2    /* a required pointer is NULL                       */
+#define FWB_E_LAUNCH 3     /* the CUDA launch failed (cudaGetLastError)        */
+#define FWB_E_CAPACITY 4   /* a size exceeds a stated maximum                  */
+
+#define FWB_STATUS_LABEL_RANGE 1   /* some label y[r] is outside [0, C)          */
+#define FWB_STATUS_NONFINITE 2     /* some row maximum is NaN or +-inf           */
+
+/* Library version, "major.minor.patch". */
+FWB_API const char* fw_version(void);
+
+/* Human-readable text for an FWB_* return code. */
+FWB_API const char* fw_error_string(int code);
+
+/*
+ * Fused forward + backward: per-row threshold search, loss and the dense
+ * gradient, in one pass that reads z once and writes grad once.
+ *   grad[r, j] = grad_scale * ((1/kappa_r) 1[z_rj > h*_r] - 1[j == y_r])
+ * grad has the same row stride `ld` as z (columns C..ld-1 are not written).
+ * grad_scale is 1/B for reduction "mean", 1 for "sum" and "none".
+ * Replaces the pair fw_radix_forward_small + fw_radix_backward_small and the
+ * pair fw_radix_forward + fw_radix_backward of the reference
+ * (src/cuda/fw_radix_argmax.cu:1381-1414, :1417-1496, :1536-1559, :1591-1608,
+ * bound in src/cuda/binding.cpp:3-6), and the forward of the CPU autograd
+ * function (src/cpu/fw_cpu.cpp:722-733).
+ */
+FWB_API int fw_fused_fwd_bwd(const float* z, const int64_t* y, int64_t B, int64_t C,
+                     int64_t ld, float grad_scale, float* grad, float* H,
+                     float* loss, int32_t* kappa, int32_t* status,
+                     void* stream);
+
+/*
+ * Forward producing the boolean support mask (uint8, [B, C] contiguous):
+ * mask[r, j] = 1[z_rj > h*_r].  Replaces fw_radix_forward_small
+ * (src/cuda/fw_radix_argmax.cu:1381-1414; binding.cpp:5,11); the reference
+ * returns the same mask as `selected_logits`.
+ */
+FWB_API int fw_forward_mask(const float* z, const int64_t* y, int64_t B, int64_t C,
+                    int64_t ld, float* H, float* loss, int32_t* kappa,
+                    uint8_t* mask, int32_t* status, void* stream);
+
+/*
+ * Dense gradient from a support mask: grad[r, j] = grad_scale *
+ * (mask[r, j] / kappa[r] - 1[j == y[r]]), grad row stride C.
+ * Replaces fw_radix_backward_small (src/cuda/fw_radix_argmax.cu:1591-1608,
+ * kernel :1561-1589; binding.cpp:6,12).
+ */
+FWB_API int fw_backward_mask(const int64_t* y, const uint8_t* mask,
+                     const int32_t* kappa, int64_t B, int64_t C,
+                     float grad_scale, float* grad, int32_t* status,
+                     void* stream);
+
+/*
+ * Forward producing the support as a candidate list: for row r,
+ * cand_val[r*C + p] / cand_idx[r*C + p] for p < cand_count[r] hold the value
+ * and column of every z_rj > h*_r (cand_count[r] == kappa[r]; order
+ * unspecified).  Replaces fw_radix_forward (src/cuda/fw_radix_argmax.cu:
+ * 1417-1496; binding.cpp:3,9), whose candidate_buffer / candidate_indices /
+ * candidate_counts outputs have this meaning and layout.
+ */
+FWB_API int fw_forward_candidates(const float* z, const int64_t* y, int64_t B,
+                          int64_t C, int64_t ld, float* H, float* loss,
+                          int32_t* kappa, float* cand_val, int32_t* cand_idx,
+                          int32_t* cand_count, int32_t* status, void* stream);
+
+/*
+ * Dense gradient from a candidate list: grad = 0, then for every candidate
+ * p < cand_count[r] with cand_val > H[r]: grad[r, cand_idx] =
+ * grad_scale / kappa[r]; finally grad[r, y[r]] -= grad_scale.  grad row
+ * stride C.  Replaces fw_radix_backward (src/cuda/fw_radix_argmax.cu:
+ * 1536-1559, kernel :1498-1534; binding.cpp:4,10).
+ */
+FWB_API int fw_backward_candidates(const float* cand_val, const int32_t* cand_idx,
+                           const int32_t* cand_count, const float* H,
+                           const int32_t* kappa, const int64_t* y, int64_t B,
+                           int64_t C, float grad_scale, float* grad,
+                           int32_t* status, void* stream);
+
+/*
+ * Backward scaling by the upstream gradient, read on the device (no host
+ * sync).  Row r of grad (row stride ld, C columns) is multiplied by
+ * grad_output[per_row ? r : 0] / assumed_scale; rows whose factor is exactly
+ * 1 are not touched, and inside a touched row only the non-zero entries are
+ * rewritten.  Replaces the host-synchronising scaling of the CPU autograd
+ * backward (src/cpu/fw_cpu.cpp:734-740).
+ */
+FWB_API int fw_scale_grad(float* grad, const float* grad_output, int per_row,
+                  float assumed_scale, int64_t B, int64_t C, int64_t ld,
+                  void* stream);
+
+/*
+ * Deterministic (fixed-order, fp64) reduction out[0] = scale * sum_r loss[r].
+ * Gives the "mean" (scale 1/B) and "sum" (scale 1) values of the reference
+ * (reference_impl.py:28-31, src/cuda/fw_radix_argmax.cu:1411,1493,
+ * src/cpu/fw_cpu.cpp:729-732).
+ */
+FWB_API int fw_loss_reduce(const float* loss, int64_t B, double scale, float* out,
+                   void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FWLOSS_B200_H */

@@ -1,0 +1,188 @@
+"""Seeded parity cases shared by the fixture generator and the tests.
+
+Each case is (name, generator) where generator() -> (z float32 [B, C],
+y int64 [B]) as numpy arrays, fully determined by its seed.  The coverage
+follows what the reference's CPU test suite is described to cover
+(src/cpu/README.md "Files": ties, constant, sorted, two-level and outlier
+inputs, magnitudes up to 1e30, K from 1 to 40,000) plus the GPU-specific
+shapes: every warp-tier slot width, unaligned row strides, the streaming
+tier with and without clusters, and dense rows that take the radix path.
+"""
+import numpy as np
+
+
+def _rng(seed):
+    return np.random.default_rng(seed)
+
+
+def _labels(rng, B, C):
+    return rng.integers(0, C, B).astype(np.int64)
+
+
+def gauss(B, C, sigma=1.0, seed=0):
+    def g():
+        r = _rng(seed)
+        z = (r.standard_normal((B, C)) * sigma).astype(np.float32)
+        return z, _labels(r, B, C)
+    return g
+
+
+def levels(B, C, lv, seed=0):
+    def g():
+        r = _rng(seed)
+        z = np.asarray(lv, dtype=np.float32)[r.integers(0, len(lv), (B, C))]
+        return z, _labels(r, B, C)
+    return g
+
+
+def constant(B, C, v=0.5, seed=0):
+    def g():
+        r = _rng(seed)
+        return np.full((B, C), v, dtype=np.float32), _labels(r, B, C)
+    return g
+
+
+def sorted_rows(B, C, seed=0):
+    def g():
+        r = _rng(seed)
+        z = np.sort(r.standard_normal((B, C)).astype(np.float32) * 0.3, axis=1)
+        z[1::2] = z[1::2, ::-1]
+        return np.ascontiguousarray(z), _labels(r, B, C)
+    return g
+
+
+def two_level(B, C, seed=0):
+    def g():
+        r = _rng(seed)
+        a = r.standard_normal(B).astype(np.float32)[:, None]
+        gap = r.uniform(0.0, 1.5, B).astype(np.float32)[:, None]
+        hi = r.random((B, C)) < 0.3
+        z = np.where(hi, a, a - gap).astype(np.float32)
+        return z, _labels(r, B, C)
+    return g
+
+
+def outliers(B, C, seed=0):
+    def g():
+        r = _rng(seed)
+        z = r.standard_normal((B, C)).astype(np.float32)
+        cols = r.integers(0, C, B)
+        z[np.arange(B), cols] = np.where(np.arange(B) % 2 == 0, 1e3, -1e3).astype(np.float32)
+        return z, _labels(r, B, C)
+    return g
+
+
+def magnitude(B, C, scale, seed=0):
+    def g():
+        r = _rng(seed)
+        z = (r.standard_normal((B, C)) * scale).astype(np.float32)
+        # duplicated maxima at huge magnitude: S_k - 1 == S_k in float64
+        z[0, : max(1, C // 3)] = z[0].max()
+        return z, _labels(r, B, C)
+    return g
+
+
+def signed_zeros(B, C, seed=0):
+    def g():
+        r = _rng(seed)
+        z = r.choice(np.array([0.0, -0.0, -0.5, -1.0, 0.25], dtype=np.float32), (B, C))
+        z[: B // 2, :] = np.where(r.random((B // 2, C)) < 0.5, np.float32(0.0), np.float32(-0.0))
+        return z.astype(np.float32), _labels(r, B, C)
+    return g
+
+
+def neg_inf(B, C, seed=0):
+    def g():
+        r = _rng(seed)
+        z = r.standard_normal((B, C)).astype(np.float32)
+        z[r.random((B, C)) < 0.4] = -np.inf
+        z[:, 0] = r.standard_normal(B).astype(np.float32)  # at least one finite per row
+        return z, _labels(r, B, C)
+    return g
+
+
+def exact_ties(seed=0):
+    """Rows where z_(k+1) == h_k exactly (first-argmax must stop at k)."""
+    def g():
+        rows = [
+            [3.5, 2.5, 0.0, -1.0],          # h1 = 2.5 == z2 -> kappa 1
+            [1.0, 0.0, 0.0, 0.0],           # h1 = 0 == z2
+            [2.0, 2.0, 1.5, -3.0],          # h2 = 1.5 == z3 -> kappa 2
+            [0.0, -0.0, -1.0, -1.0],        # +-0 tie, h2 = -0.5
+            [0.5, 0.5, 0.5, 0.5],           # constant -> kappa 4
+            [1.0, 1.0, 0.0, 0.0],           # h2 = 0.5 > 0 -> kappa 2
+            [4.0, 3.0, 3.0, 3.0],           # h1 = 3 == z2 -> kappa 1
+            [0.75, 0.25, -0.25, -0.25],     # h2 = 0 > -0.25 -> kappa 2
+        ]
+        z = np.asarray(rows, dtype=np.float32)
+        return z, _rng(seed).integers(0, 4, len(rows)).astype(np.int64)
+    return g
+
+
+def parity_cases(full=False):
+    """List of (name, generator).  `full` adds the slow, large cases."""
+    cases = []
+    for C in list(range(1, 65)) + [100, 127, 128, 129, 255, 256, 257, 511, 512, 513, 1000, 1023,
+                                   1024, 1025, 2047, 2048]:
+        cases.append((f"gauss_C{C}", gauss(6, C, 1.0, seed=C)))
+    for C in [2049, 3000, 4096, 10000, 31623, 32000, 100000]:
+        cases.append((f"gauss_mid_C{C}", gauss(5, C, 1.0, seed=C)))
+    cases += [
+        ("ties_C128", levels(64, 128, [-3.5, -2.5, -1.5, -0.5, 0.5, 1.5, 2.5, 3.5], seed=1)),
+        ("ties_C5000", levels(16, 5000, [-1.0, 0.0, 1.0, 2.0], seed=2)),
+        ("ties_C40000", levels(4, 40000, [0.0, 0.5, 1.0], seed=3)),
+        ("const_C1", constant(4, 1)),
+        ("const_C5", constant(4, 5, 2.0)),
+        ("const_C1000", constant(4, 1000, -3.0)),
+        ("const_C3000", constant(3, 3000, 1.0)),
+        ("const_C40000", constant(2, 40000, 0.1)),
+        ("sorted_C1000", sorted_rows(8, 1000, seed=4)),
+        ("sorted_C40000", sorted_rows(4, 40000, seed=5)),
+        ("twolevel_C700", two_level(16, 700, seed=6)),
+        ("twolevel_C20000", two_level(8, 20000, seed=7)),
+        ("outlier_C1000", outliers(8, 1000, seed=8)),
+        ("outlier_C50000", outliers(4, 50000, seed=9)),
+        ("mag1e30_C64", magnitude(6, 64, 1e30, seed=10)),
+        ("mag1e30_C5000", magnitude(4, 5000, 1e30, seed=11)),
+        ("mag1e20_C300", magnitude(6, 300, 1e20, seed=12)),
+        ("mag1e-30_C300", magnitude(6, 300, 1e-30, seed=13)),
+        ("zeros_C100", signed_zeros(16, 100, seed=14)),
+        ("zeros_C9000", signed_zeros(4, 9000, seed=15)),
+        ("neginf_C500", neg_inf(8, 500, seed=16)),
+        ("neginf_C12000", neg_inf(4, 12000, seed=17)),
+        ("dense_s1e-3_C1000", gauss(8, 1000, 1e-3, seed=18)),
+        ("dense_s1e-3_C40000", gauss(4, 40000, 1e-3, seed=19)),
+        ("dense_s1e-2_C100000", gauss(2, 100000, 1e-2, seed=20)),
+        ("dense_s1e-1_C3000", gauss(8, 3000, 1e-1, seed=21)),
+        ("exact_ties", exact_ties(seed=22)),
+    ]
+    if full:
+        cases += [
+            ("dense_s1e-3_C300000", gauss(2, 300000, 1e-3, seed=23)),
+            ("gauss_C1000000", gauss(2, 1000000, 1.0, seed=24)),
+        ]
+    return cases
+
+
+def nonfinite_cases():
+    """Rows whose maximum is NaN or +-inf (policy, not reference, semantics)."""
+    def g_nan():
+        r = _rng(30)
+        z = r.standard_normal((6, 3000)).astype(np.float32)
+        z[0, 17] = np.nan
+        z[1, 5] = np.inf
+        z[2, :] = -np.inf
+        z[3, 2999] = np.nan
+        z[3, 10] = np.inf
+        return z, _labels(r, 6, 3000)
+
+    def g_small():
+        r = _rng(31)
+        z = r.standard_normal((5, 40)).astype(np.float32)
+        z[0, 3] = np.nan
+        z[1, 39] = np.inf
+        z[2, :] = -np.inf
+        z[3, 0] = -np.inf
+        return z, _labels(r, 5, 40)
+
+    return [("nonfinite_C3000", g_nan), ("nonfinite_C40", g_small)]

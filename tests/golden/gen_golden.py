@@ -1,0 +1,110 @@
+"""Writes the golden fixtures of tests/golden/ from the REFERENCE itself.
+
+Run in a container that has the reference checkout (FW_REF_PATH, default
+/root/reference) and the reference CPU extension built by oracle/build.py:
+
+    python tests/golden/gen_golden.py
+
+Outputs (inputs are not stored: every case regenerates them from its seed,
+see tests/cases.py and fwloss_b200.workloads):
+  reference_outputs.npz  per case: what reference_impl.FWLoss (float32, CPU;
+                         reference_impl.py:3-35) and the reference CPU
+                         extension (src/cpu/fw_cpu.cpp, fw_loss_grad) return:
+                         kappa, H, per-row loss and the gradient (sparse:
+                         row, col, value) for reduction "mean".
+  kat_kbar.json          the known answers the reference ships: the `kbar`
+                         (mean kappa over 32 rows) of every (distribution,
+                         sigma, K) in benchmarks/cpu_benchmarks/results/*.json,
+                         with the generation parameters of
+                         benchmarks/cpu_benchmarks/bench_cpu_e2e.py:7-41.
+"""
+import json
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, REPO)
+sys.path.insert(0, os.path.join(REPO, "tests"))
+sys.path.insert(0, os.path.join(REPO, "fast-familywise-loss_b200"))
+REF = os.environ.get("FW_REF_PATH", "/root/reference")
+sys.path.insert(0, REF)
+
+import torch  # noqa: E402
+
+import cases  # noqa: E402
+from fwloss_b200 import workloads  # noqa: E402
+from oracle import ref_cpu  # noqa: E402
+import reference_impl  # noqa: E402  (the reference's own module)
+
+CONFIG_ROWS = {"cfg0": 256, "cfg1": 512, "cfg2": 64, "cfg3": 2048, "cfg4": 8}
+
+
+def sparse(g):
+    r, c = np.nonzero(g)
+    return r.astype(np.int32), c.astype(np.int32), g[r, c].astype(np.float32)
+
+
+def reference_outputs(z, y):
+    B, C = z.shape
+    zt = torch.from_numpy(z).clone().requires_grad_(True)
+    yt = torch.from_numpy(y)
+    H, losses, mean, kappas = reference_impl.FWLoss(C, reduction="mean")(zt, yt)
+    mean.backward()
+    L, G, K = ref_cpu.ref_loss_grad(z, y, 1.0 / B)
+    out = {
+        "kappa_ref32": kappas.numpy().astype(np.int64),
+        "H_ref32": H.detach().numpy().astype(np.float32),
+        "loss_ref32": losses.detach().numpy().astype(np.float32),
+        "mean_ref32": np.float32(mean.item()),
+        "kappa_cpu": K.astype(np.int64),
+        "loss_cpu": L.astype(np.float64),
+    }
+    for tag, g in (("grad_ref32", zt.grad.numpy()), ("grad_cpu", G)):
+        r, c, v = sparse(g)
+        out[tag + "_r"], out[tag + "_c"], out[tag + "_v"] = r, c, v
+    return out
+
+
+def all_cases():
+    for name, gen in cases.parity_cases(full=False):
+        yield name, gen
+    for name, rows in CONFIG_ROWS.items():
+        def g(name=name, rows=rows):
+            z, y = workloads.make(name, rows=rows)
+            return z.numpy(), y.numpy()
+        yield name, g
+
+
+def kat():
+    res = os.path.join(REF, "benchmarks", "cpu_benchmarks", "results")
+    out = {}
+    for fname in ("gaussian.json", "gaussian_avx2_1thread.json", "laplace.json", "mixture.json"):
+        d = json.load(open(os.path.join(res, fname)))
+        stds = list(d["runs"].keys())
+        entry = {"N": d["N"], "Ks": d["Ks"], "dist": d.get("dist", "gaussian"),
+                 "mix_mean": d.get("mix_mean", 2.0), "stds": stds, "kbar": {}}
+        for s in stds:
+            runs = d["runs"][s]["FW (ours)"]
+            assert [r["K"] for r in runs] == d["Ks"], fname
+            entry["kbar"][s] = [r["kbar"] for r in runs]
+        out[fname[:-5]] = entry
+    return out
+
+
+def main():
+    store = {}
+    for name, gen in all_cases():
+        z, y = gen()
+        for k, v in reference_outputs(z, y).items():
+            store[f"{name}/{k}"] = v
+        print(name, z.shape, flush=True)
+    np.savez_compressed(os.path.join(HERE, "reference_outputs.npz"), **store)
+    with open(os.path.join(HERE, "kat_kbar.json"), "w") as f:
+        json.dump(kat(), f, indent=1)
+
+
+if __name__ == "__main__":
+    main()

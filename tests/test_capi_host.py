@@ -1,0 +1,73 @@
+"""The C-ABI library and the drop-in module load and export what
+include/fwloss_b200.h declares; host-side argument checks return their error
+codes before any device work (CPU only)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from fwloss_b200 import capi
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include",
+                      "fwloss_b200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return re.findall(r"FWB_API\s+[\w\s\*]+?\b(fw_\w+)\s*\(", text)
+
+
+def test_library_exports_every_declared_symbol():
+    names = declared_symbols()
+    assert len(names) >= 9
+    lib = ctypes.CDLL(capi.LIB_PATH)
+    for n in names:
+        assert hasattr(lib, n), n
+    assert set(names) == set(capi.EXPORTED)
+
+
+def test_only_c_abi_is_exported():
+    import subprocess
+
+    out = subprocess.run(["nm", "-D", "--defined-only", capi.LIB_PATH], capture_output=True, text=True).stdout
+    text_syms = {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
+    assert text_syms == set(declared_symbols())
+
+
+def test_version_and_error_strings():
+    assert capi.version() == "0.1.0"
+    lib = capi.load()
+    for code in range(5):
+        assert lib.fw_error_string(code)
+    assert b"unknown" in lib.fw_error_string(99)
+
+
+def test_argument_checks_without_device():
+    lib = capi.load()
+    P = None
+    dummy = ctypes.c_void_p(16)
+    # C < 1, ld < C, B < 0 -> FWB_E_SHAPE
+    assert lib.fw_fused_fwd_bwd(dummy, dummy, 4, 0, 0, 1.0, dummy, P, P, P, P, P) == 1
+    assert lib.fw_fused_fwd_bwd(dummy, dummy, 4, 10, 9, 1.0, dummy, P, P, P, P, P) == 1
+    assert lib.fw_fused_fwd_bwd(dummy, dummy, -1, 10, 10, 1.0, dummy, P, P, P, P, P) == 1
+    assert lib.fw_forward_mask(dummy, dummy, 2, 2 ** 31, 2 ** 31, P, P, P, dummy, P, P) == 1
+    # missing required pointers -> FWB_E_POINTER
+    assert lib.fw_fused_fwd_bwd(P, dummy, 4, 10, 10, 1.0, dummy, P, P, P, P, P) == 2
+    assert lib.fw_fused_fwd_bwd(dummy, dummy, 4, 10, 10, 1.0, P, P, P, P, P, P) == 2
+    assert lib.fw_forward_candidates(dummy, dummy, 4, 10, 10, P, P, P, P, dummy, P, P, P) == 2
+    assert lib.fw_backward_mask(P, dummy, dummy, 4, 10, 1.0, dummy, P, P) == 2
+    assert lib.fw_loss_reduce(dummy, 4, 1.0, P, P) == 2
+    # an empty batch is a valid no-op (no launch)
+    assert lib.fw_fused_fwd_bwd(P, P, 0, 10, 10, 1.0, P, P, P, P, P, P) == 0
+
+
+def test_dropin_module_surface():
+    import torch  # noqa: F401
+
+    import fw_radix_cuda
+
+    for fn in ("fw_forward", "fw_backward", "fw_forward_small", "fw_backward_small"):
+        assert callable(getattr(fw_radix_cuda, fn))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        fw_radix_cuda.fw_forward_small(torch.randn(2, 5), torch.zeros(2, dtype=torch.long))

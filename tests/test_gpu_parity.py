@@ -1,0 +1,235 @@
+"""GPU parity of the CUDA kernels, called through the C ABI (ctypes), against
+the CPU oracle and the reference's own outputs (tests/golden).
+
+Contract (north star): kappa and the selected set bit-exact; H, per-row loss
+and gradient within rtol 1e-5 / atol 1e-6 (fp32).
+"""
+import numpy as np
+import pytest
+import torch
+
+import cases
+from fwloss_b200 import capi, workloads
+from oracle import fw_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-5, 1e-6
+GOLDEN = np.load(__import__("os").path.join(__import__("os").path.dirname(__file__), "golden",
+                                            "reference_outputs.npz"))
+CONFIG_ROWS = {"cfg0": 256, "cfg1": 512, "cfg2": 64, "cfg3": 2048, "cfg4": 8}
+
+
+def _to_dev(z, y, ld=None, offset=0):
+    """Device copies; ld > C gives padded rows, offset shifts the base pointer
+    off its 16-byte alignment (both force the 32-bit access path)."""
+    B, C = z.shape
+    ld = C if ld is None else ld
+    buf = torch.full((B * ld + offset + 4,), float("nan"), dtype=torch.float32, device="cuda")
+    view = buf[offset:offset + B * ld].view(B, ld)[:, :C]
+    view.copy_(torch.from_numpy(z))
+    return view, torch.from_numpy(y).cuda()
+
+
+def _fused(z, y, scale, **kw):
+    zt, yt = _to_dev(z, y, **kw)
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    grad, H, loss, kappa = capi.fused_fwd_bwd(zt, yt, scale, status=st)
+    torch.cuda.synchronize()
+    return dict(grad=grad.cpu().numpy(), H=H.cpu().numpy(), loss=loss.cpu().numpy(),
+                kappa=kappa.cpu().numpy().astype(np.int64), status=int(st.item()), z=zt)
+
+
+def _check_row_outputs(out, z, y, ref, name=""):
+    np.testing.assert_array_equal(out["kappa"], ref["kappa"], err_msg=f"{name}: kappa")
+    np.testing.assert_allclose(out["H"], ref["H"], rtol=RTOL, atol=ATOL, err_msg=f"{name}: H")
+    np.testing.assert_allclose(out["loss"], ref["loss"], rtol=RTOL, atol=ATOL, err_msg=f"{name}: loss")
+    # H is rounded toward -inf: the mask z > H is exactly the support
+    sel = (z > out["H"][:, None])
+    fin = np.isfinite(ref["M"])
+    np.testing.assert_array_equal(sel[fin].sum(1), out["kappa"][fin], err_msg=f"{name}: |z > H|")
+    np.testing.assert_array_equal(sel[fin], ref["mask"][fin], err_msg=f"{name}: support")
+
+
+def _check_golden(name, out):
+    if f"{name}/kappa_cpu" not in GOLDEN.files:
+        return
+    np.testing.assert_array_equal(out["kappa"], GOLDEN[f"{name}/kappa_cpu"], err_msg=f"{name}: kappa vs ref CPU")
+    np.testing.assert_allclose(out["loss"], GOLDEN[f"{name}/loss_cpu"], rtol=RTOL, atol=ATOL,
+                               err_msg=f"{name}: loss vs ref CPU")
+    B, C = out["grad"].shape
+    g = np.zeros((B, C), np.float32)
+    g[GOLDEN[f"{name}/grad_cpu_r"], GOLDEN[f"{name}/grad_cpu_c"]] = GOLDEN[f"{name}/grad_cpu_v"]
+    np.testing.assert_allclose(out["grad"], g, rtol=RTOL, atol=ATOL, err_msg=f"{name}: grad vs ref CPU")
+
+
+PARITY = cases.parity_cases()
+
+
+@pytest.mark.parametrize("name,gen", PARITY, ids=[n for n, _ in PARITY])
+def test_fused_matches_oracle_and_reference(name, gen):
+    z, y = gen()
+    scale = 1.0 / len(y)
+    ref = O.solve(z, y, scale)
+    out = _fused(z, y, scale)
+    _check_row_outputs(out, z, y, ref, name)
+    np.testing.assert_allclose(out["grad"], ref["grad"], rtol=RTOL, atol=ATOL, err_msg=f"{name}: grad")
+    _check_golden(name, out)
+    assert out["status"] == 0
+
+
+@pytest.mark.parametrize("name", list(CONFIG_ROWS))
+def test_configs_reduced_match_reference(name):
+    z, y = workloads.make(name, rows=CONFIG_ROWS[name])
+    z, y = z.numpy(), y.numpy()
+    ref = O.solve(z, y)
+    out = _fused(z, y, 1.0 / len(y))
+    _check_row_outputs(out, z, y, ref, name)
+    np.testing.assert_allclose(out["grad"], ref["grad"], rtol=RTOL, atol=ATOL)
+    _check_golden(name, out)
+    # the float32 reference_impl agrees bit-exactly on kappa for all five configs
+    np.testing.assert_array_equal(out["kappa"], GOLDEN[f"{name}/kappa_ref32"])
+    np.testing.assert_allclose(out["H"], GOLDEN[f"{name}/H_ref32"], rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(out["loss"], GOLDEN[f"{name}/loss_ref32"], rtol=RTOL, atol=ATOL)
+
+
+@pytest.mark.parametrize("C", [3, 64, 100, 1000, 1001, 2048, 3001, 40000])
+@pytest.mark.parametrize("layout", ["padded", "offset"])
+def test_unaligned_rows(C, layout):
+    z, y = cases.gauss(7, C, 1.0, seed=100 + C)()
+    ref = O.solve(z, y, 0.5)
+    kw = {"ld": C + 3} if layout == "padded" else {"offset": 1}
+    out = _fused(z, y, 0.5, **kw)
+    _check_row_outputs(out, z, y, ref, f"C{C}-{layout}")
+    np.testing.assert_allclose(out["grad"], ref["grad"], rtol=RTOL, atol=ATOL)
+
+
+@pytest.mark.parametrize("name,gen", cases.nonfinite_cases(), ids=[n for n, _ in cases.nonfinite_cases()])
+def test_nonfinite_policy(name, gen):
+    z, y = gen()
+    ref = O.solve(z, y, 1.0)
+    out = _fused(z, y, 1.0)
+    np.testing.assert_array_equal(out["kappa"], ref["kappa"])
+    np.testing.assert_array_equal(out["H"], ref["H"])  # NaN == NaN here
+    np.testing.assert_allclose(out["loss"], ref["loss"].astype(np.float32), rtol=RTOL, atol=ATOL, equal_nan=True)
+    np.testing.assert_allclose(out["grad"], ref["grad"], rtol=RTOL, atol=ATOL)
+    assert out["status"] & capi.FWB_STATUS_NONFINITE
+
+
+def test_label_out_of_range_flags_and_nan():
+    z, y = cases.gauss(4, 300, 1.0, seed=5)()
+    y = y.copy()
+    y[1] = -1
+    y[2] = 300
+    out = _fused(z, y, 1.0)
+    assert out["status"] & capi.FWB_STATUS_LABEL_RANGE
+    assert np.isnan(out["loss"][1]) and np.isnan(out["loss"][2])
+    assert np.isfinite(out["loss"][[0, 3]]).all()
+    # rows with a bad label still get their support, with no label term
+    ref = O.solve(z, np.where((y < 0) | (y >= 300), 0, y), 1.0)
+    np.testing.assert_array_equal(out["kappa"], ref["kappa"])
+    g = out["grad"]
+    np.testing.assert_allclose(g[1].sum(), 1.0, rtol=1e-5)
+
+
+@pytest.mark.parametrize("name,gen", [c for c in PARITY if c[0] in (
+    "gauss_C1", "gauss_C37", "gauss_C1000", "gauss_mid_C10000", "ties_C128", "dense_s1e-3_C1000",
+    "dense_s1e-3_C40000", "const_C40000", "exact_ties", "mag1e30_C5000", "gauss_mid_C31623",
+    "neginf_C12000", "zeros_C9000")])
+def test_mask_and_candidate_forms(name, gen):
+    z, y = gen()
+    B, C = z.shape
+    ref = O.solve(z, y, 1.0 / B)
+    zt, yt = _to_dev(z, y)
+    H, loss, kappa, mask = capi.forward_mask(zt, yt)
+    g_mask = capi.backward_mask(yt, mask, kappa, 1.0 / B)
+    H2, loss2, kappa2, cv, ci, cc = capi.forward_candidates(zt, yt)
+    g_cand = capi.backward_candidates(cv, ci, cc, H2, kappa2, yt, 1.0 / B)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(mask.cpu().numpy(), ref["mask"])
+    np.testing.assert_array_equal(kappa.cpu().numpy(), ref["kappa"])
+    np.testing.assert_array_equal(kappa2.cpu().numpy(), ref["kappa"])
+    np.testing.assert_array_equal(cc.cpu().numpy(), ref["kappa"])
+    np.testing.assert_array_equal(H.cpu().numpy(), H2.cpu().numpy())
+    np.testing.assert_allclose(loss.cpu().numpy(), ref["loss"], rtol=RTOL, atol=ATOL)
+    # candidate rows hold exactly the support
+    cvn, cin, ccn = cv.cpu().numpy(), ci.cpu().numpy(), cc.cpu().numpy()
+    for r in range(B):
+        cols = np.sort(cin[r, : ccn[r]])
+        np.testing.assert_array_equal(cols, np.nonzero(ref["mask"][r])[0])
+        np.testing.assert_array_equal(cvn[r, : ccn[r]], z[r, cin[r, : ccn[r]]])
+    np.testing.assert_allclose(g_mask.cpu().numpy(), ref["grad"], rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(g_cand.cpu().numpy(), ref["grad"], rtol=RTOL, atol=ATOL)
+
+
+def test_scale_grad_and_loss_reduce():
+    z, y = cases.gauss(64, 5000, 1.0, seed=9)()
+    ref = O.solve(z, y, 1.0)
+    zt, yt = _to_dev(z, y)
+    grad, H, loss, kappa = capi.fused_fwd_bwd(zt, yt, 1.0)
+    go = torch.linspace(-2.0, 2.0, 64, device="cuda")
+    go[5] = 1.0
+    capi.scale_grad(grad, go, True, 1.0)
+    np.testing.assert_allclose(grad.cpu().numpy(), ref["grad"] * go.cpu().numpy()[:, None],
+                               rtol=RTOL, atol=ATOL)
+    s = capi.loss_reduce(loss, 1.0 / 64)
+    np.testing.assert_allclose(s.item(), ref["loss"].mean(), rtol=1e-6)
+    g2, *_ = capi.fused_fwd_bwd(zt, yt, 1.0 / 64)
+    capi.scale_grad(g2, torch.tensor([3.0], device="cuda"), False, 1.0)
+    np.testing.assert_allclose(g2.cpu().numpy(), ref["grad"] * 3.0 / 64, rtol=RTOL, atol=ATOL)
+
+
+def test_empty_batch_is_noop():
+    z = torch.empty((0, 100), dtype=torch.float32, device="cuda")
+    y = torch.empty((0,), dtype=torch.int64, device="cuda")
+    grad, H, loss, kappa = capi.fused_fwd_bwd(z, y, 1.0)
+    torch.cuda.synchronize()
+    assert grad.shape == (0, 100)
+
+
+def test_deterministic_repeat():
+    z, y = workloads.make("cfg2", rows=256)
+    zt, yt = z.cuda(), y.cuda()
+    a = capi.fused_fwd_bwd(zt, yt, 1.0 / 256)
+    b = capi.fused_fwd_bwd(zt, yt, 1.0 / 256)
+    for u, v in zip(a, b):
+        assert torch.equal(u, v)
+
+
+def _full_size_properties(z, y, out_grad, H, loss, kappa, scale, sample_rows=48):
+    """Size-independent checks at full configuration size (on the device),
+    plus an oracle comparison on a random sample of rows."""
+    B, C = z.shape
+    sel = z > H[:, None]
+    assert torch.equal(sel.sum(1).to(torch.int32), kappa)
+    nz = (out_grad != 0).sum(1)
+    ysel = sel[torch.arange(B, device=z.device), y]
+    assert torch.equal(nz, kappa.long() + (~ysel).long() - (ysel & (kappa == 1)).long())
+    rs = out_grad.double().sum(1)
+    assert rs.abs().max().item() <= 1e-6 * max(1.0, scale * 10)
+    # threshold optimality: sum_j max(z_j - h, 0) == 1 at h = H (up to the round-down of H)
+    f = torch.clamp(z.double() - H.double()[:, None], min=0).sum(1)
+    ulp = torch.abs(H.double()) * 2.0 ** -23 + 1e-30
+    assert ((f - 1.0).abs() <= kappa.double() * ulp * 2 + 1e-9).all()
+    zy = z[torch.arange(B, device=z.device), y].double()
+    np.testing.assert_allclose(loss.double().cpu().numpy(), (1.0 - zy + H.double()).cpu().numpy(),
+                               rtol=RTOL, atol=ATOL)
+    g = torch.Generator().manual_seed(0)
+    rows = torch.randperm(B, generator=g)[:sample_rows].sort().values
+    zs = z[rows.cuda()].cpu().numpy()
+    ys = y[rows.cuda()].cpu().numpy()
+    ref = O.solve(zs, ys, scale)
+    np.testing.assert_array_equal(kappa[rows.cuda()].cpu().numpy(), ref["kappa"])
+    np.testing.assert_allclose(out_grad[rows.cuda()].cpu().numpy(), ref["grad"], rtol=RTOL, atol=ATOL)
+
+
+@pytest.mark.parametrize("name", ["cfg1", "cfg2", "cfg3", "cfg4"])
+def test_full_size_configs(name):
+    z, y = workloads.make(name)
+    z, y = z.cuda(), y.cuda()
+    B = z.shape[0]
+    grad, H, loss, kappa = capi.fused_fwd_bwd(z, y, 1.0 / B)
+    torch.cuda.synchronize()
+    _full_size_properties(z, y, grad, H, loss, kappa, 1.0 / B)
+    del grad
+    torch.cuda.empty_cache()
