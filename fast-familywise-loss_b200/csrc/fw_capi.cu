@@ -2,8 +2,8 @@
 // Declarations and semantics: include/fwloss_b200.h.
 //
 // Tier selection by class count C (the tile shape scales with C):
-//   C <= 2048          warp per row, row in registers (fw_warp_tier.cuh);
-//                      VW = ceil(C / 128) 16-byte slots per lane.
+//   C <= 2048          a group of 8/16/32 lanes per row, row in registers
+//                      (fw_warp_tier.cuh).
 //   C  > 2048          CTA per row (CS = 1) or a cluster of CS = 2/4/8 CTAs per
 //                      row when there are too few rows to fill the GPU
 //                      (fw_stream_tier.cuh).
@@ -64,9 +64,9 @@ cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, int cluster,
 }
 
 // ------------------------------------------------------------- warp tier
-template <int VW, bool VEC, int OUT>
+template <int G, int NS4, bool VEC, int OUT>
 cudaError_t launch_warp_tier(const RowArgs& a, cudaStream_t st) {
-  auto k = fw_warp_rows_kernel<VW, VEC, OUT>;
+  auto k = fw_warp_rows_kernel<G, NS4, VEC, OUT>;
   static int occ = 0;  // resident CTAs per SM for this instance
   if (occ == 0) {
     int o = 0;
@@ -74,20 +74,24 @@ cudaError_t launch_warp_tier(const RowArgs& a, cudaStream_t st) {
       o = 1;
     occ = o;
   }
-  const int64_t need = (a.B + kWarpTierWarps - 1) / kWarpTierWarps;
+  const int64_t rows_per_block = (int64_t)kWarpTierWarps * (32 / G);
+  const int64_t need = (a.B + rows_per_block - 1) / rows_per_block;
   const int64_t cap = (int64_t)sm_count() * occ;
   const int grid = (int)(need < cap ? need : cap);
   return launch(k, dim3(grid), dim3(kWarpTierThreads), 1, st, a);
 }
 
+// Lanes per row G and 16-byte slots per lane NS4 by class count:
+//   C <= 64: 8 x 2,  <= 128: 8 x 4,  <= 256: 16 x 4,  <= 512: 32 x 4,
+//   <= 1024: 32 x 8,  <= 2048: 32 x 16.
 template <bool VEC, int OUT>
 cudaError_t dispatch_warp_vw(const RowArgs& a, cudaStream_t st) {
-  const int64_t slots = (a.C + 127) / 128;
-  if (slots <= 1) return launch_warp_tier<1, VEC, OUT>(a, st);
-  if (slots <= 2) return launch_warp_tier<2, VEC, OUT>(a, st);
-  if (slots <= 4) return launch_warp_tier<4, VEC, OUT>(a, st);
-  if (slots <= 8) return launch_warp_tier<8, VEC, OUT>(a, st);
-  return launch_warp_tier<16, VEC, OUT>(a, st);
+  if (a.C <= 64) return launch_warp_tier<8, 2, VEC, OUT>(a, st);
+  if (a.C <= 128) return launch_warp_tier<8, 4, VEC, OUT>(a, st);
+  if (a.C <= 256) return launch_warp_tier<16, 4, VEC, OUT>(a, st);
+  if (a.C <= 512) return launch_warp_tier<32, 4, VEC, OUT>(a, st);
+  if (a.C <= 1024) return launch_warp_tier<32, 8, VEC, OUT>(a, st);
+  return launch_warp_tier<32, 16, VEC, OUT>(a, st);
 }
 
 // ----------------------------------------------------------- stream tier

@@ -96,43 +96,96 @@ __device__ __forceinline__ int warp_excl_scan(int v, int lane) {
 
 __device__ __forceinline__ unsigned lanemask_lt(int lane) { return (1u << lane) - 1u; }
 
+// Lane-group helpers: a "group" is G consecutive lanes of a warp (G = 4, 8,
+// 16 or 32) with member mask gmask; xor offsets below G never leave the group.
+template <int G>
+__device__ __forceinline__ float group_max_nan(float v, unsigned gmask) {
+#pragma unroll
+  for (int o = G / 2; o > 0; o >>= 1) v = max_nan(v, __shfl_xor_sync(gmask, v, o));
+  return v;
+}
+
+template <int G>
+__device__ __forceinline__ double group_sum(double v, unsigned gmask) {
+#pragma unroll
+  for (int o = G / 2; o > 0; o >>= 1) v += __shfl_xor_sync(gmask, v, o);
+  return v;
+}
+
+template <int G>
+__device__ __forceinline__ int group_sum(int v, unsigned gmask) {
+  if constexpr (G == 32) {
+    return __reduce_add_sync(gmask, v);
+  } else {
+#pragma unroll
+    for (int o = G / 2; o > 0; o >>= 1) v += __shfl_xor_sync(gmask, v, o);
+    return v;
+  }
+}
+
+template <int G>
+__device__ __forceinline__ unsigned group_min(unsigned v, unsigned gmask) {
+#pragma unroll
+  for (int o = G / 2; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(gmask, v, o));
+  return v;
+}
+
+template <int G>
+__device__ __forceinline__ int group_excl_scan(int v, int li, unsigned gmask) {
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < G; o <<= 1) {
+    const int t = __shfl_up_sync(gmask, x, o, G);
+    if (li >= o) x += t;
+  }
+  return x - v;
+}
+
+// fp32 threshold of a shifted threshold t: H(t) = M + t rounded toward -inf
+// in two directed steps, so that for every fp32 x:  x > H(t) <=> x > M + t
+// (exact real).  Selection always uses this predicate, which makes the
+// support, kappa and the emitted H consistent by construction.
+__device__ __forceinline__ float threshold_fp32(float M, double tau) {
+  return __double2float_rd(__dadd_rd((double)M, tau));
+}
+
 // Exact threshold on a candidate list (Michelot's fixed-point iteration,
-// i.e. Newton's method from below on f(t) = sum_j max(d_j - t, 0) - 1).
+// i.e. Newton's method from below on f(t) = sum_j max(z_j - M - t, 0) - 1).
 // `L` holds n >= 1 candidate logits (a superset of the support; it always
-// contains the row maximum).  Iterates T <- {d in T : d > tau_T},
-// tau_T = (sum_T d - 1)/|T| until |T| stops changing.  The sets are nested
-// and each step removes at least one element, so at most n + 1 passes run.
-// At the fixed point every d in T is > tau_T and every removed d is <= tau_T,
-// hence T is exactly the support and tau_T = h* - M.  All lanes of the warp
-// must call it; all return the same (tau, kappa).
-__device__ __forceinline__ void michelot_list(const float* L, int n, double Md,
-                                              int lane, double& tau,
-                                              int& kappa) {
+// contains the row maximum).  Iterates T <- {x in T : x > H(t_T)},
+// t_T = (sum_T (x - M) - 1)/|T| until |T| stops changing.  The sets are
+// nested and each step removes at least one element, so at most n + 1
+// passes run.  At the fixed point every x in T exceeds M + t and every
+// removed x does not, hence T is exactly the support and t = h* - M.  Sums
+// are fp64 in a fixed order (lane-strided, then a butterfly), so the result
+// is deterministic.  All G lanes of the group must call it with the same
+// arguments; all return the same (tau, kappa).
+template <int G>
+__device__ __forceinline__ void michelot_list(const float* L, int n, float M, int li,
+                                              unsigned gmask, double& tau, int& kappa) {
+  const double Md = (double)M;
   double t = -CUDART_INF;
+  float Ht = -CUDART_INF_F;
   int prev = -1;
   for (int it = 0; it <= n; ++it) {
     double s = 0.0;
     int c = 0;
-    for (int i = lane; i < n; i += 32) {
-      const double d = (double)L[i] - Md;
-      if (d > t) { s += d; ++c; }
+    for (int i = li; i < n; i += G) {
+      const float x = L[i];
+      if (x > Ht) { s += (double)x - Md; ++c; }
     }
-    c = warp_sum(c);
-    s = warp_sum(s);
+    c = group_sum<G>(c, gmask);
+    s = group_sum<G>(s, gmask);
     if (c == prev) break;
     prev = c;
     t = (s - 1.0) / (double)c;
+    Ht = threshold_fp32(M, t);
   }
   tau = t;
   kappa = prev;
 }
 
-// fp32 outputs of a solved row.  H rounds M + tau toward -inf in two directed
-// steps, so for every fp32 x: x > H <=> x > M + tau (exact real).
-__device__ __forceinline__ float threshold_fp32(float M, double tau) {
-  return __double2float_rd(__dadd_rd((double)M, tau));
-}
-
+// Per-row loss 1 - z_y + h* from the shifted threshold.
 __device__ __forceinline__ float row_loss(float M, double tau, float zy) {
   return (float)(1.0 + ((double)M - (double)zy) + tau);
 }

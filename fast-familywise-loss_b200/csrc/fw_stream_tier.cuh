@@ -429,13 +429,14 @@ __global__ void __launch_bounds__(kST)
     const int n = s.nsolve;
     double tau;
     int kap;
-    michelot_list(s.sz, n, Md, lane, tau, kap);
+    michelot_list<32>(s.sz, n, M, lane, kFull, tau, kap);
+    const float Hf = threshold_fp32(M, tau);  // x > Hf <=> x in the support
     if (OUT == kOutGrad) {
       const float inv = (float)((double)a.scale / (double)kap);
       bool ysel = false;
       for (int k = lane; k < n; k += 32) {
         const int col = s.si[k];
-        if ((double)s.sz[k] - Md > tau) {
+        if (s.sz[k] > Hf) {
           float gv = inv;
           if (col == yc) {
             gv -= a.scale;
@@ -448,14 +449,14 @@ __global__ void __launch_bounds__(kST)
       if (lane == 0 && yok && !ysel) gr[yc] = -a.scale;
     } else if (OUT == kOutMask) {
       for (int k = lane; k < n; k += 32)
-        if ((double)s.sz[k] - Md > tau) mr[s.si[k]] = 1;
+        if (s.sz[k] > Hf) mr[s.si[k]] = 1;
     } else {
       float* cv = a.cand_val + row * C;
       int32_t* ci = a.cand_idx + row * C;
       int pos0 = 0;
       for (int k0 = 0; k0 < n; k0 += 32) {
         const int k = k0 + lane;
-        const bool sel = (k < n) && ((double)s.sz[k] - Md > tau);
+        const bool sel = (k < n) && (s.sz[k] > Hf);
         const unsigned b = __ballot_sync(kFull, sel);
         if (sel) {
           const int pos = pos0 + __popc(b & lanemask_lt(lane));
@@ -468,7 +469,7 @@ __global__ void __launch_bounds__(kST)
     }
     if (lane == 0) {
       const float zy = yok ? zr[yc] : CUDART_NAN_F;
-      if (a.H) a.H[row] = threshold_fp32(M, tau);
+      if (a.H) a.H[row] = Hf;
       if (a.loss) a.loss[row] = yok ? row_loss(M, tau, zy) : CUDART_NAN_F;
       if (a.kappa) a.kappa[row] = kap;
       if (!yok) raise_status(a.status, 1);

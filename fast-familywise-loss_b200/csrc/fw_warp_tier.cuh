@@ -1,25 +1,26 @@
-// Warp-per-row tier (C <= 32 * 4 * VW): the whole row sits in registers of
-// one warp, so the row is read from HBM once and its output is written once,
-// with no shared-memory traffic except the short candidate list.
+// Register tier (C <= 2048): a group of G lanes (G = 8, 16 or 32; 32/G rows
+// per warp) holds one row in registers, so the row is read from HBM once and
+// its output written once, with no shared-memory traffic except the short
+// candidate list.
 //
 // Per row:
 //   1. load (128-bit when rows are 16-byte aligned), M = NaN-propagating max
-//      by shuffles;
-//   2. candidates z > t0 are compacted into a per-warp list by an exclusive
+//      by xor shuffles inside the group;
+//   2. candidates z > t0 are compacted into a per-group list by an exclusive
 //      shuffle scan (the common case: a handful of elements);
-//   3. exact threshold: Michelot's fixed point on the list
-//      (michelot_list), or on the registers when the list would overflow
-//      (near-constant rows where most of the row is within 1 of the max);
-//   4. output written straight from the registers: the gradient
-//      grad_scale * ((1/kappa) [z > h*] - e_y), the support mask, or the
-//      support list.
+//   3. exact threshold: Michelot's fixed point on the list (michelot_list),
+//      or on the registers when the list would overflow (near-constant rows
+//      where most of the row is within 1 of the max);
+//   4. output straight from the registers with the fp32 predicate z > H:
+//      the gradient grad_scale * ((1/kappa) [z > h*] - e_y), the support mask,
+//      or the support list.
 //
 // Reference counterpart: fw_radix_shared_kernel<8,32,100> / <8,128,5000>
 // (src/cuda/fw_radix_argmax.cu:1192-1356) followed by fw_backward_mask_kernel
-// (:1561-1589).  The reference finds h* by up to four 8-bit digit passes
-// with four shared-memory atomics per element and then needs a second kernel
-// for the gradient; here the threshold comes from the candidate list and the
-// gradient is written by the same warp.
+// (:1561-1589).  The reference finds h* by up to four 8-bit digit passes with
+// four shared-memory atomics per element, writes a bool mask, and needs a
+// second kernel to turn it into the gradient; here the threshold comes from
+// the candidate list and the gradient is written by the same lanes.
 #pragma once
 
 #include <climits>
@@ -30,35 +31,137 @@ namespace fwb200 {
 
 constexpr int kWarpTierThreads = 256;
 constexpr int kWarpTierWarps = kWarpTierThreads / 32;
-constexpr int kWarpListCap = 128;
+constexpr int kWarpListCap = 128;  // list entries per warp, split between its groups
 
-// Column of register slot (i, j) of `lane`.  Aligned rows use 128-bit loads
-// (lane owns 4 consecutive columns per slot group); unaligned rows use
-// lane-contiguous scalar loads so that every load instruction is coalesced.
-template <bool VEC>
-__device__ __forceinline__ int warp_slot_col(int i, int j, int lane) {
-  return VEC ? ((i * 32 + lane) * 4 + j) : ((i * 4 + j) * 32 + lane);
+// Column of register slot (i, j) of lane `li` of a G-lane group.  Aligned rows
+// use 128-bit loads (a lane owns 4 consecutive columns per slot); unaligned
+// rows use lane-contiguous scalar loads so every load instruction coalesces.
+template <int G, bool VEC>
+__device__ __forceinline__ int group_slot_col(int i, int j, int li) {
+  return VEC ? ((i * G + li) * 4 + j) : ((i * 4 + j) * G + li);
 }
 
-template <int VW, bool VEC, int OUT>
-__global__ void __launch_bounds__(kWarpTierThreads)
+// Stores the 4 values of register slot i (columns group_slot_col(i, 0..3)).
+template <int G, bool VEC>
+__device__ __forceinline__ void warp_tier_store4(float* gr, int i, int li, int C, const float (&g)[4]) {
+  if (VEC) {
+    const int c0 = (i * G + li) * 4;
+    if (c0 + 3 < C) {
+      *reinterpret_cast<float4*>(gr + c0) = make_float4(g[0], g[1], g[2], g[3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (c0 + j < C) gr[c0 + j] = g[j];
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = group_slot_col<G, false>(i, j, li);
+      if (c < C) gr[c] = g[j];
+    }
+  }
+}
+
+template <int G, bool VEC>
+__device__ __forceinline__ void warp_tier_store4_mask(uint8_t* mr, int i, int li, int C, int mask_vec,
+                                                      const uint8_t (&b)[4]) {
+  const int c0 = (i * G + li) * 4;
+  if (VEC && mask_vec && c0 + 3 < C) {
+    *reinterpret_cast<uchar4*>(mr + c0) = make_uchar4(b[0], b[1], b[2], b[3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = group_slot_col<G, VEC>(i, j, li);
+      if (c < C) mr[c] = b[j];
+    }
+  }
+}
+
+// Row whose maximum is NaN or +-inf: kappa = 1 at the first column holding
+// the maximum (the first NaN for NaN rows), H = M, loss = 1 - z_y + M (fp32).
+template <int G, int NS4, bool VEC, int OUT>
+__device__ __forceinline__ void warp_tier_nonfinite(const RowArgs& a, int64_t row, const float (&v)[NS4 * 4],
+                                                 float m, int li, unsigned gmask, int yc, float zy) {
+  const int C = (int)a.C;
+  const bool isn = (m != m);
+  unsigned best = 0xffffffffu;
+#pragma unroll
+  for (int i = 0; i < NS4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = group_slot_col<G, VEC>(i, j, li);
+      const float x = v[4 * i + j];
+      if (c < C && (isn ? (x != x) : (x == m))) best = min(best, (unsigned)c);
+    }
+  const int jstar = (int)group_min<G>(best, gmask);
+  if (OUT == kOutGrad) {
+    float* gr = a.grad + row * a.ld;
+#pragma unroll
+    for (int i = 0; i < NS4; ++i) {
+      float g[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) g[j] = (group_slot_col<G, VEC>(i, j, li) == jstar) ? a.scale : 0.0f;
+      warp_tier_store4<G, VEC>(gr, i, li, C, g);
+    }
+    if (yc >= 0) {
+      __syncwarp(gmask);
+      if (li == 0) gr[yc] = ((yc == jstar) ? a.scale : 0.0f) - a.scale;
+    }
+  } else if (OUT == kOutMask) {
+    uint8_t* mr = a.mask + row * a.C;
+#pragma unroll
+    for (int i = 0; i < NS4; ++i) {
+      uint8_t b[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = (group_slot_col<G, VEC>(i, j, li) == jstar) ? 1 : 0;
+      warp_tier_store4_mask<G, VEC>(mr, i, li, C, a.mask_vec, b);
+    }
+  } else if (li == 0) {
+    a.cand_val[row * a.C] = a.z[row * a.ld + jstar];
+    a.cand_idx[row * a.C] = jstar;
+    if (a.cand_count) a.cand_count[row] = 1;
+  }
+  if (li == 0) {
+    if (a.H) a.H[row] = m;
+    if (a.loss) a.loss[row] = (yc >= 0) ? (1.0f - zy + m) : CUDART_NAN_F;
+    if (a.kappa) a.kappa[row] = 1;
+    if (yc < 0) raise_status(a.status, 1);
+    raise_status(a.status, 2);
+  }
+}
+
+// Resident CTAs per SM the register budget is sized for (no spills): 3 (85
+// registers) up to 16 values per lane, 2 (128) at 32, 1 at 64.
+template <int NS4>
+constexpr int warp_tier_min_blocks() {
+  return NS4 <= 4 ? 3 : (NS4 <= 8 ? 2 : 1);
+}
+
+template <int G, int NS4, bool VEC, int OUT>
+__global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS4>())
     fw_warp_rows_kernel(RowArgs a) {
-  constexpr int NS = VW * 4;
+  constexpr int NS = NS4 * 4;           // register slots per lane
+  constexpr int RPW = 32 / G;           // rows per warp
+  constexpr int CAPG = kWarpListCap / RPW;
   __shared__ float s_list[kWarpTierWarps][kWarpListCap];
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
+  const int gi = lane / G;              // group in warp
+  const int li = lane % G;              // lane in group
+  const unsigned gmask = (G == 32) ? kFull : (((1u << G) - 1u) << (gi * G));
+  float* L = &s_list[wib][gi * CAPG];
   const int C = (int)a.C;
-  const int64_t nwarps = (int64_t)gridDim.x * kWarpTierWarps;
+  const int64_t ngroups = (int64_t)gridDim.x * kWarpTierWarps * RPW;
 
-  for (int64_t row = (int64_t)blockIdx.x * kWarpTierWarps + wib; row < a.B;
-       row += nwarps) {
+  for (int64_t row = ((int64_t)blockIdx.x * kWarpTierWarps + wib) * RPW + gi; row < a.B;
+       row += ngroups) {
     const float* zr = a.z + row * a.ld;
     const int64_t ylab = a.y[row];
     float v[NS];
 #pragma unroll
-    for (int i = 0; i < VW; ++i) {
+    for (int i = 0; i < NS4; ++i) {
       if (VEC) {
-        const int c0 = (i * 32 + lane) * 4;
+        const int c0 = (i * G + li) * 4;
         if (c0 + 3 < C) {
           const float4 q = ld_stream4(zr + c0);
           v[4 * i + 0] = q.x;
@@ -73,7 +176,7 @@ __global__ void __launch_bounds__(kWarpTierThreads)
       } else {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const int c = warp_slot_col<false>(i, j, lane);
+          const int c = group_slot_col<G, false>(i, j, li);
           v[4 * i + j] = (c < C) ? ld_stream1(zr + c) : -CUDART_INF_F;
         }
       }
@@ -82,161 +185,113 @@ __global__ void __launch_bounds__(kWarpTierThreads)
     float m = -CUDART_INF_F;
 #pragma unroll
     for (int s = 0; s < NS; ++s) m = max_nan(m, v[s]);
-    m = warp_max_nan(m);
+    m = group_max_nan<G>(m, gmask);
 
     const bool yok = (ylab >= 0 && ylab < a.C);
     const int yc = yok ? (int)ylab : -1;
-    const bool nonfinite = !isfinite(m);  // warp-uniform
-    const double Md = (double)m;
-    const float t0 = __fsub_rd(m, 1.0f);
-    double tau = 0.0;
-    int kap = 1;
-    int jstar = -1;
+    const float zy = yok ? __ldg(zr + yc) : CUDART_NAN_F;
 
-    if (!nonfinite) {
-      int c = 0;
+    if (!isfinite(m)) {  // group-uniform; rare
+      warp_tier_nonfinite<G, NS4, VEC, OUT>(a, row, v, m, li, gmask, yc, zy);
+      continue;
+    }
+
+    const float t0 = __fsub_rd(m, 1.0f);
+    int c = 0;
 #pragma unroll
-      for (int s = 0; s < NS; ++s) c += (v[s] > t0) ? 1 : 0;
-      const int tot = warp_sum(c);
-      if (tot <= kWarpListCap) {
-        int off = warp_excl_scan(c, lane);
-        float* L = s_list[wib];
+    for (int s = 0; s < NS; ++s) c += (v[s] > t0) ? 1 : 0;
+    const int n = group_sum<G>(c, gmask);
+    double tau;
+    int kap;
+    if (n == 1) {
+      // a unique maximum and nothing else above M - 1: h* = M - 1, kappa = 1
+      tau = -1.0;
+      kap = 1;
+    } else if (n <= CAPG) {
+      int off = group_excl_scan<G>(c, li, gmask);
+      if (c > 0) {
 #pragma unroll
         for (int s = 0; s < NS; ++s)
           if (v[s] > t0) L[off++] = v[s];
-        __syncwarp();
-        michelot_list(L, tot, Md, lane, tau, kap);
-        __syncwarp();
-      } else {
-        // Same fixed point, evaluated on the registers (dense rows).
-        double t = -CUDART_INF;
-        int prev = -1;
-        for (int it = 0; it <= C; ++it) {
-          double sum = 0.0;
-          int cnt = 0;
-#pragma unroll
-          for (int s = 0; s < NS; ++s) {
-            const double d = (double)v[s] - Md;
-            if (v[s] > t0 && d > t) { sum += d; ++cnt; }
-          }
-          cnt = warp_sum(cnt);
-          sum = warp_sum(sum);
-          if (cnt == prev) break;
-          prev = cnt;
-          t = (sum - 1.0) / (double)cnt;
-        }
-        tau = t;
-        kap = prev;
       }
+      __syncwarp(gmask);
+      michelot_list<G>(L, n, m, li, gmask, tau, kap);
+      __syncwarp(gmask);
     } else {
-      // Non-finite maximum: kappa = 1 at the first column holding the
-      // maximum (the first NaN for NaN rows), H = M.
-      const bool isn = (m != m);
-      int best = INT_MAX;
+      // Same fixed point, evaluated on the registers (dense rows).
+      const double Md = (double)m;
+      double t = -CUDART_INF;
+      float Ht = t0;
+      int prev = -1;
+      for (int it = 0; it <= C; ++it) {
+        double sum = 0.0;
+        int cnt = 0;
 #pragma unroll
-      for (int i = 0; i < VW; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int c = warp_slot_col<VEC>(i, j, lane);
-          const float x = v[4 * i + j];
-          if (c < C && (isn ? (x != x) : (x == m))) best = min(best, c);
-        }
-      jstar = (int)__reduce_min_sync(kFull, (unsigned)best);
+        for (int s = 0; s < NS; ++s)
+          if (v[s] > Ht) { sum += (double)v[s] - Md; ++cnt; }
+        cnt = group_sum<G>(cnt, gmask);
+        sum = group_sum<G>(sum, gmask);
+        if (cnt == prev) break;
+        prev = cnt;
+        t = (sum - 1.0) / (double)cnt;
+        Ht = fmaxf(threshold_fp32(m, t), t0);
+      }
+      tau = t;
+      kap = prev;
     }
-
-    const float zy = yok ? __ldg(zr + yc) : CUDART_NAN_F;
-
-    auto selected = [&](int s, int c) -> bool {
-      if (nonfinite) return c == jstar;
-      return v[s] > t0 && ((double)v[s] - Md) > tau;
-    };
+    const float Hf = threshold_fp32(m, tau);  // x > Hf <=> x in the support
 
     if (OUT == kOutGrad) {
-      const float inv = nonfinite ? a.scale : (float)((double)a.scale / (double)kap);
+      // Support entries first; the label entry is rewritten by lane 0 after a
+      // group barrier (which orders the two stores to that address).
+      const float inv = (float)((double)a.scale / (double)kap);
       float* gr = a.grad + row * a.ld;
 #pragma unroll
-      for (int i = 0; i < VW; ++i) {
+      for (int i = 0; i < NS4; ++i) {
         float g[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int c = warp_slot_col<VEC>(i, j, lane);
-          g[j] = selected(4 * i + j, c) ? inv : 0.0f;
-          if (c == yc) g[j] -= a.scale;
-        }
-        if (VEC) {
-          const int c0 = (i * 32 + lane) * 4;
-          if (c0 + 3 < C) {
-            *reinterpret_cast<float4*>(gr + c0) = make_float4(g[0], g[1], g[2], g[3]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              if (c0 + j < C) gr[c0 + j] = g[j];
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int c = warp_slot_col<false>(i, j, lane);
-            if (c < C) gr[c] = g[j];
-          }
-        }
+        for (int j = 0; j < 4; ++j) g[j] = (v[4 * i + j] > Hf) ? inv : 0.0f;
+        warp_tier_store4<G, VEC>(gr, i, li, C, g);
+      }
+      if (yok) {
+        __syncwarp(gmask);
+        if (li == 0) gr[yc] = ((zy > Hf) ? inv : 0.0f) - a.scale;
       }
     } else if (OUT == kOutMask) {
       uint8_t* mr = a.mask + row * a.C;
 #pragma unroll
-      for (int i = 0; i < VW; ++i) {
+      for (int i = 0; i < NS4; ++i) {
         uint8_t b[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          b[j] = selected(4 * i + j, warp_slot_col<VEC>(i, j, lane)) ? 1 : 0;
-        if (VEC && a.mask_vec && (i * 32 + lane) * 4 + 3 < C) {
-          const int c0 = (i * 32 + lane) * 4;
-          *reinterpret_cast<uchar4*>(mr + c0) = make_uchar4(b[0], b[1], b[2], b[3]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int c = warp_slot_col<VEC>(i, j, lane);
-            if (c < C) mr[c] = b[j];
-          }
-        }
+        for (int j = 0; j < 4; ++j) b[j] = (v[4 * i + j] > Hf) ? 1 : 0;
+        warp_tier_store4_mask<G, VEC>(mr, i, li, C, a.mask_vec, b);
       }
     } else {  // kOutCand
       int cnt = 0;
 #pragma unroll
-      for (int i = 0; i < VW; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          cnt += selected(4 * i + j, warp_slot_col<VEC>(i, j, lane)) ? 1 : 0;
-      int off = warp_excl_scan(cnt, lane);
+      for (int s = 0; s < NS; ++s) cnt += (v[s] > Hf) ? 1 : 0;
+      int off = group_excl_scan<G>(cnt, li, gmask);
       float* cv = a.cand_val + row * a.C;
       int32_t* ci = a.cand_idx + row * a.C;
+      if (cnt > 0) {
 #pragma unroll
-      for (int i = 0; i < VW; ++i)
+        for (int i = 0; i < NS4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int c = warp_slot_col<VEC>(i, j, lane);
-          if (selected(4 * i + j, c)) {
-            cv[off] = v[4 * i + j];
-            ci[off] = c;
-            ++off;
-          }
-        }
-      if (lane == 0 && a.cand_count) a.cand_count[row] = kap;
+          for (int j = 0; j < 4; ++j)
+            if (v[4 * i + j] > Hf) {
+              cv[off] = v[4 * i + j];
+              ci[off] = group_slot_col<G, VEC>(i, j, li);
+              ++off;
+            }
+      }
+      if (li == 0 && a.cand_count) a.cand_count[row] = kap;
     }
 
-    if (lane == 0) {
-      float Hf, lf;
-      if (!nonfinite) {
-        Hf = threshold_fp32(m, tau);
-        lf = yok ? row_loss(m, tau, zy) : CUDART_NAN_F;
-      } else {
-        Hf = m;
-        lf = yok ? (1.0f - zy + m) : CUDART_NAN_F;
-      }
+    if (li == 0) {
       if (a.H) a.H[row] = Hf;
-      if (a.loss) a.loss[row] = lf;
+      if (a.loss) a.loss[row] = yok ? row_loss(m, tau, zy) : CUDART_NAN_F;
       if (a.kappa) a.kappa[row] = kap;
       if (!yok) raise_status(a.status, 1);
-      if (nonfinite) raise_status(a.status, 2);
     }
   }
 }
