@@ -66,17 +66,20 @@ cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, int cluster,
 // ------------------------------------------------------------- warp tier
 template <int G, int NS4, bool VEC, int OUT>
 cudaError_t launch_warp_tier(const RowArgs& a, cudaStream_t st) {
-  auto k = fw_warp_rows_kernel<G, NS4, VEC, OUT>;
-  static int occ = 0;  // resident CTAs per SM for this instance
-  if (occ == 0) {
-    int o = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k, kWarpTierThreads, 0) != cudaSuccess || o < 1)
-      o = 1;
-    occ = o;
+  // every 16-byte slot fully inside or outside the row: one predicate per slot
+  const bool full4 = VEC && (a.C % 4 == 0);
+  auto k = full4 ? fw_warp_rows_kernel<G, NS4, VEC, OUT, true> : fw_warp_rows_kernel<G, NS4, VEC, OUT, false>;
+  static int occ[2] = {0, 0};  // resident CTAs per SM of the two instances
+  int& o = occ[full4 ? 1 : 0];
+  if (o == 0) {
+    int r = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, k, kWarpTierThreads, 0) != cudaSuccess || r < 1)
+      r = 1;
+    o = r;
   }
   const int64_t rows_per_block = (int64_t)kWarpTierWarps * (32 / G);
   const int64_t need = (a.B + rows_per_block - 1) / rows_per_block;
-  const int64_t cap = (int64_t)sm_count() * occ;
+  const int64_t cap = (int64_t)sm_count() * o;
   const int grid = (int)(need < cap ? need : cap);
   return launch(k, dim3(grid), dim3(kWarpTierThreads), 1, st, a);
 }

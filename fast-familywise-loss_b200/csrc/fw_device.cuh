@@ -160,7 +160,9 @@ __device__ __forceinline__ float threshold_fp32(float M, double tau) {
 // are fp64 in a fixed order (lane-strided, then a butterfly), so the result
 // is deterministic.  All G lanes of the group must call it with the same
 // arguments; all return the same (tau, kappa).
-template <int G>
+// CAP > 0 bounds n (n <= CAP) and turns the per-lane loop into CAP/G
+// predicated steps; CAP == 0 means any n.
+template <int G, int CAP = 0>
 __device__ __forceinline__ void michelot_list(const float* L, int n, float M, int li,
                                               unsigned gmask, double& tau, int& kappa) {
   const double Md = (double)M;
@@ -170,9 +172,18 @@ __device__ __forceinline__ void michelot_list(const float* L, int n, float M, in
   for (int it = 0; it <= n; ++it) {
     double s = 0.0;
     int c = 0;
-    for (int i = li; i < n; i += G) {
-      const float x = L[i];
-      if (x > Ht) { s += (double)x - Md; ++c; }
+    if constexpr (CAP > 0) {
+#pragma unroll
+      for (int k = 0; k < CAP / G; ++k) {
+        const int i = li + k * G;
+        const float x = (i < n) ? L[i] : -CUDART_INF_F;
+        if (x > Ht) { s += (double)x - Md; ++c; }
+      }
+    } else {
+      for (int i = li; i < n; i += G) {
+        const float x = L[i];
+        if (x > Ht) { s += (double)x - Md; ++c; }
+      }
     }
     c = group_sum<G>(c, gmask);
     s = group_sum<G>(s, gmask);

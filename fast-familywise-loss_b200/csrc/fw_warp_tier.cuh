@@ -42,9 +42,12 @@ __device__ __forceinline__ int group_slot_col(int i, int j, int li) {
 }
 
 // Stores the 4 values of register slot i (columns group_slot_col(i, 0..3)).
-template <int G, bool VEC>
+template <int G, bool VEC, bool FULL4 = false>
 __device__ __forceinline__ void warp_tier_store4(float* gr, int i, int li, int C, const float (&g)[4]) {
-  if (VEC) {
+  if (VEC && FULL4) {
+    const int c0 = (i * G + li) * 4;
+    if (c0 < C) *reinterpret_cast<float4*>(gr + c0) = make_float4(g[0], g[1], g[2], g[3]);
+  } else if (VEC) {
     const int c0 = (i * G + li) * 4;
     if (c0 + 3 < C) {
       *reinterpret_cast<float4*>(gr + c0) = make_float4(g[0], g[1], g[2], g[3]);
@@ -62,7 +65,7 @@ __device__ __forceinline__ void warp_tier_store4(float* gr, int i, int li, int C
   }
 }
 
-template <int G, bool VEC>
+template <int G, bool VEC, bool FULL4 = false>
 __device__ __forceinline__ void warp_tier_store4_mask(uint8_t* mr, int i, int li, int C, int mask_vec,
                                                       const uint8_t (&b)[4]) {
   const int c0 = (i * G + li) * 4;
@@ -137,7 +140,9 @@ constexpr int warp_tier_min_blocks() {
   return NS4 <= 4 ? 3 : (NS4 <= 8 ? 2 : 1);
 }
 
-template <int G, int NS4, bool VEC, int OUT>
+// FULL4 (with VEC): C % 4 == 0, so every 16-byte slot is entirely inside or
+// entirely outside the row and loads/stores need one predicate per slot.
+template <int G, int NS4, bool VEC, int OUT, bool FULL4>
 __global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS4>())
     fw_warp_rows_kernel(RowArgs a) {
   constexpr int NS = NS4 * 4;           // register slots per lane
@@ -160,7 +165,15 @@ __global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS4>())
     float v[NS];
 #pragma unroll
     for (int i = 0; i < NS4; ++i) {
-      if (VEC) {
+      if (VEC && FULL4) {
+        const int c0 = (i * G + li) * 4;
+        float4 q = make_float4(-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F);
+        if (c0 < C) q = ld_stream4(zr + c0);
+        v[4 * i + 0] = q.x;
+        v[4 * i + 1] = q.y;
+        v[4 * i + 2] = q.z;
+        v[4 * i + 3] = q.w;
+      } else if (VEC) {
         const int c0 = (i * G + li) * 4;
         if (c0 + 3 < C) {
           const float4 q = ld_stream4(zr + c0);
@@ -215,7 +228,7 @@ __global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS4>())
           if (v[s] > t0) L[off++] = v[s];
       }
       __syncwarp(gmask);
-      michelot_list<G>(L, n, m, li, gmask, tau, kap);
+      michelot_list<G, CAPG>(L, n, m, li, gmask, tau, kap);
       __syncwarp(gmask);
     } else {
       // Same fixed point, evaluated on the registers (dense rows).
@@ -251,7 +264,7 @@ __global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS4>())
         float g[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) g[j] = (v[4 * i + j] > Hf) ? inv : 0.0f;
-        warp_tier_store4<G, VEC>(gr, i, li, C, g);
+        warp_tier_store4<G, VEC, FULL4>(gr, i, li, C, g);
       }
       if (yok) {
         __syncwarp(gmask);
@@ -264,7 +277,7 @@ __global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS4>())
         uint8_t b[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) b[j] = (v[4 * i + j] > Hf) ? 1 : 0;
-        warp_tier_store4_mask<G, VEC>(mr, i, li, C, a.mask_vec, b);
+        warp_tier_store4_mask<G, VEC, FULL4>(mr, i, li, C, a.mask_vec, b);
       }
     } else {  // kOutCand
       int cnt = 0;
