@@ -61,19 +61,22 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-graph", action="store_true", help="launch steps eagerly")
+    p.add_argument("--dtype", default="f32", choices=["f32", "bf16", "f16"],
+                   help="logits/gradient element type (the metric is defined on f32)")
     return p.parse_args()
 
 
-def workload_desc(name, B, C, world):
+def workload_desc(name, B, C, world, esize=4):
     kinds = {"cfg0": "N(0,1)", "cfg1": "N(0,1) +4 at label", "cfg2": "Student-t(3) x2",
              "cfg3": "8 levels + 1% signed zeros", "cfg4": "N(0,1) +8 at a non-label class"}
     return {
-        "workload": f"{name}: FWLoss fwd+bwd, B={B} x C={C}, fp32 logits {kinds.get(name, '')}, int64 labels",
+        "workload": f"{name}: FWLoss fwd+bwd, B={B} x C={C}, {dict([(4, 'fp32'), (2, '16-bit')])[esize]} "
+                    f"logits {kinds.get(name, '')}, int64 labels",
         "rows_per_gpu": B, "classes": C, "global_batch": B * world,
         "parallelism": f"row-sharded dp{world}" + (" + scalar NCCL all-reduce" if world > 1 else ""),
-        "l2": f"inputs {B * C * 4 / 1e6:.1f} MB logits + {B * C * 4 / 1e6:.1f} MB gradient per step"
-              + (" (> 3x the 126 MB L2, no flush needed)" if B * C * 4 > 3 * L2_BYTES else
-                 f" (rotating over {min(64, -(-3 * L2_BYTES // (B * C * 4)))} input copies)"),
+        "l2": f"inputs {B * C * esize / 1e6:.1f} MB logits + {B * C * esize / 1e6:.1f} MB gradient per step"
+              + (" (> 3x the 126 MB L2, no flush needed)" if B * C * esize > 3 * L2_BYTES else
+                 f" (rotating over {min(64, -(-3 * L2_BYTES // (B * C * esize)))} input copies)"),
     }
 
 
@@ -264,9 +267,12 @@ def run_ours(a):
     # inputs: rank 0 gets the configuration itself, other ranks the same recipe
     # with their own seed (weak scaling: every rank owns B distinct rows)
     z_cpu, y_cpu = workloads.make_rank(a.config, rank)
+    tdt = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[a.dtype]
+    esize = torch.tensor([], dtype=tdt).element_size()
+    z_cpu = z_cpu.to(tdt)
     # inputs larger than L2 (126 MB): small configurations rotate over enough
     # copies that 3x the L2 size is touched between two uses of one copy
-    copies = 1 if B * C * 4 > 3 * L2_BYTES else min(64, -(-3 * L2_BYTES // (B * C * 4)))
+    copies = 1 if B * C * esize > 3 * L2_BYTES else min(64, -(-3 * L2_BYTES // (B * C * esize)))
     zs = [z_cpu.to(dev) for _ in range(copies)]
     y = y_cpu.to(dev)
     Bg = B * world
@@ -365,7 +371,7 @@ def run_ours(a):
     kd1.record(stream)
     torch.cuda.synchronize(dev)
     k_ms = kd0.elapsed_time(kd1) / a.steps
-    alg_bytes = B * (8 * C + 12)
+    alg_bytes = B * (2 * esize * C + 12)
     achieved = alg_bytes / (k_ms / 1e3) / 1e9
     peak, peak_kind = measured_peak()
 
@@ -407,7 +413,7 @@ def run_ours(a):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e_ms = float(t.item())
     e2e = {"value": Bg * ne / (e_ms / 1e3), "unit": UNIT,
-           "h2d_bytes_per_step": int(zh.numel() * 4 + yh.numel() * 8), "d2h_bytes_per_step": 4,
+           "h2d_bytes_per_step": int(zh.numel() * esize + yh.numel() * 8), "d2h_bytes_per_step": 4,
            "ms_per_step": e_ms / ne, "api": "fwloss_b200.familywise_loss(mean).backward()"}
 
     cpu = None
@@ -423,10 +429,10 @@ def run_ours(a):
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": ms / a.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": dict(workload_desc(a.config, B, C, world),
+            "scaling": "weak", "vs_baseline": None, "dtype": a.dtype, "data": "synthetic",
+            "config": dict(workload_desc(a.config, B, C, world, esize),
                            launch="CUDA-graph replay of each step" if use_graph else "eager"),
-            "hbm_gbs": alg_bytes * world * a.steps / (ms / 1e3) / 1e9 / world,
+            "hbm_gbs": alg_bytes * a.steps / (ms / 1e3) / 1e9,
             "roofline": {"bound": "hbm", "kernel": "fw_stream_rows_kernel" if C > 2048 else "fw_warp_rows_kernel",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "traffic": profile_traffic(a.config),

@@ -107,37 +107,35 @@ __global__ void __launch_bounds__(kAuxThreads)
 // Row r of grad *= grad_output[per_row ? r : 0] / assumed.  Rows whose factor
 // is exactly 1 are skipped; for finite factors only non-zero entries are
 // rewritten (the gradient has kappa + 1 of them), for non-finite factors the
-// whole row is (0 * inf = NaN, as in a dense multiply).
+// whole row is (0 * inf = NaN, as in a dense multiply).  T is the gradient's
+// element type; 16-byte slots when vec.
+template <class T>
 __global__ void __launch_bounds__(kAuxThreads)
-    fw_scale_grad_kernel(float* __restrict__ grad,
-                         const float* __restrict__ grad_output, int per_row,
-                         float assumed, int64_t B, int64_t C, int64_t ld,
-                         int vec) {
+    fw_scale_grad_kernel(T* __restrict__ grad, const float* __restrict__ grad_output, int per_row,
+                         float assumed, int64_t B, int64_t C, int64_t ld, int vec) {
+  constexpr int EPS = Elem<T>::kEPS;
   for (int64_t r = blockIdx.x; r < B; r += gridDim.x) {
     const float f = grad_output[per_row ? r : 0] / assumed;
     if (f == 1.0f) continue;
     const bool dense = !isfinite(f);
-    float* gr = grad + r * ld;
+    T* gr = grad + r * ld;
+    int64_t done = 0;
     if (vec) {
-      for (int64_t q = threadIdx.x; q < C / 4; q += blockDim.x) {
-        float4 g = *reinterpret_cast<const float4*>(gr + 4 * q);
-        if (dense || g.x != 0.f || g.y != 0.f || g.z != 0.f || g.w != 0.f) {
-          g.x *= f;
-          g.y *= f;
-          g.z *= f;
-          g.w *= f;
-          *reinterpret_cast<float4*>(gr + 4 * q) = g;
+      for (int64_t q = threadIdx.x; q < C / EPS; q += blockDim.x) {
+        const uint4 u = *reinterpret_cast<const uint4*>(gr + EPS * q);
+        if (dense || (u.x | u.y | u.z | u.w) != 0u) {
+          float g[EPS];
+          unpack16<T>(u, g);
+#pragma unroll
+          for (int j = 0; j < EPS; ++j) g[j] *= f;
+          *reinterpret_cast<uint4*>(gr + EPS * q) = pack16<T>(g);
         }
       }
-      for (int64_t c = 4 * (C / 4) + threadIdx.x; c < C; c += blockDim.x) {
-        const float g = gr[c];
-        if (dense || g != 0.f) gr[c] = g * f;
-      }
-    } else {
-      for (int64_t c = threadIdx.x; c < C; c += blockDim.x) {
-        const float g = gr[c];
-        if (dense || g != 0.f) gr[c] = g * f;
-      }
+      done = EPS * (C / EPS);
+    }
+    for (int64_t c = done + threadIdx.x; c < C; c += blockDim.x) {
+      const float g = ld_elem(gr + c);
+      if (dense || g != 0.f) st_elem(gr + c, g * f);
     }
   }
 }

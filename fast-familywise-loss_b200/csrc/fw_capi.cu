@@ -64,13 +64,15 @@ cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, int cluster,
 }
 
 // ------------------------------------------------------------- warp tier
-template <int G, int NS4, bool VEC, int OUT>
+template <class T, int G, int NS, bool VEC, int OUT>
 cudaError_t launch_warp_tier(const RowArgs& a, cudaStream_t st) {
-  // every 16-byte slot fully inside or outside the row: one predicate per slot
-  const bool full4 = VEC && (a.C % 4 == 0);
-  auto k = full4 ? fw_warp_rows_kernel<G, NS4, VEC, OUT, true> : fw_warp_rows_kernel<G, NS4, VEC, OUT, false>;
+  // FULLV: every 16-byte slot fully inside or outside the row (one predicate
+  // per slot); only meaningful for 16-byte accesses
+  const bool fullv = VEC && (a.C % Elem<T>::kEPS == 0);
+  auto k = fullv ? fw_warp_rows_kernel<T, G, NS, VEC, OUT, VEC>
+                 : fw_warp_rows_kernel<T, G, NS, VEC, OUT, false>;
   static int occ[2] = {0, 0};  // resident CTAs per SM of the two instances
-  int& o = occ[full4 ? 1 : 0];
+  int& o = occ[fullv ? 1 : 0];
   if (o == 0) {
     int r = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, k, kWarpTierThreads, 0) != cudaSuccess || r < 1)
@@ -84,23 +86,24 @@ cudaError_t launch_warp_tier(const RowArgs& a, cudaStream_t st) {
   return launch(k, dim3(grid), dim3(kWarpTierThreads), 1, st, a);
 }
 
-// Lanes per row G and 16-byte slots per lane NS4 by class count:
-//   C <= 64: 8 x 2,  <= 128: 8 x 4,  <= 256: 16 x 4,  <= 512: 32 x 4,
-//   <= 1024: 32 x 8,  <= 2048: 32 x 16.
-template <bool VEC, int OUT>
-cudaError_t dispatch_warp_vw(const RowArgs& a, cudaStream_t st) {
-  if (a.C <= 64) return launch_warp_tier<8, 2, VEC, OUT>(a, st);
-  if (a.C <= 128) return launch_warp_tier<8, 4, VEC, OUT>(a, st);
-  if (a.C <= 256) return launch_warp_tier<16, 4, VEC, OUT>(a, st);
-  if (a.C <= 512) return launch_warp_tier<32, 4, VEC, OUT>(a, st);
-  if (a.C <= 1024) return launch_warp_tier<32, 8, VEC, OUT>(a, st);
-  return launch_warp_tier<32, 16, VEC, OUT>(a, st);
+// Lanes per row G and register values per lane NV by class count:
+//   C <= 64: 8 x 8,  <= 128: 8 x 16,  <= 256: 16 x 16,  <= 512: 32 x 16,
+//   <= 1024: 32 x 32,  <= 2048: 32 x 64  (NS = NV / EPS 16-byte slots).
+template <class T, bool VEC, int OUT>
+cudaError_t dispatch_warp(const RowArgs& a, cudaStream_t st) {
+  constexpr int E = Elem<T>::kEPS;
+  if (a.C <= 64) return launch_warp_tier<T, 8, 8 / E, VEC, OUT>(a, st);
+  if (a.C <= 128) return launch_warp_tier<T, 8, 16 / E, VEC, OUT>(a, st);
+  if (a.C <= 256) return launch_warp_tier<T, 16, 16 / E, VEC, OUT>(a, st);
+  if (a.C <= 512) return launch_warp_tier<T, 32, 16 / E, VEC, OUT>(a, st);
+  if (a.C <= 1024) return launch_warp_tier<T, 32, 32 / E, VEC, OUT>(a, st);
+  return launch_warp_tier<T, 32, 64 / E, VEC, OUT>(a, st);
 }
 
 // ----------------------------------------------------------- stream tier
-template <int CS, bool VEC, int OUT>
+template <class T, int CS, bool VEC, int OUT>
 cudaError_t launch_stream_tier(const RowArgs& a, cudaStream_t st) {
-  auto k = fw_stream_rows_kernel<CS, VEC, OUT>;
+  auto k = fw_stream_rows_kernel<T, CS, VEC, OUT>;
   const int64_t grid = a.B * CS;
   return launch(k, dim3((unsigned)grid), dim3(kST), CS, st, a);
 }
@@ -114,24 +117,24 @@ int choose_cluster(int64_t B, int64_t C) {
   return cs;
 }
 
-template <bool VEC, int OUT>
-cudaError_t dispatch_stream_cs(const RowArgs& a, cudaStream_t st) {
+template <class T, bool VEC, int OUT>
+cudaError_t dispatch_stream(const RowArgs& a, cudaStream_t st) {
   switch (choose_cluster(a.B, a.C)) {
-    case 8: return launch_stream_tier<8, VEC, OUT>(a, st);
-    case 4: return launch_stream_tier<4, VEC, OUT>(a, st);
-    case 2: return launch_stream_tier<2, VEC, OUT>(a, st);
-    default: return launch_stream_tier<1, VEC, OUT>(a, st);
+    case 8: return launch_stream_tier<T, 8, VEC, OUT>(a, st);
+    case 4: return launch_stream_tier<T, 4, VEC, OUT>(a, st);
+    case 2: return launch_stream_tier<T, 2, VEC, OUT>(a, st);
+    default: return launch_stream_tier<T, 1, VEC, OUT>(a, st);
   }
 }
 
-template <int OUT>
+template <class T, int OUT>
 int run_rows(const RowArgs& a, cudaStream_t st, bool vec) {
   if (a.B == 0) return FWB_OK;
   cudaError_t e;
   if (a.C <= kWarpTierMaxC)
-    e = vec ? dispatch_warp_vw<true, OUT>(a, st) : dispatch_warp_vw<false, OUT>(a, st);
+    e = vec ? dispatch_warp<T, true, OUT>(a, st) : dispatch_warp<T, false, OUT>(a, st);
   else
-    e = vec ? dispatch_stream_cs<true, OUT>(a, st) : dispatch_stream_cs<false, OUT>(a, st);
+    e = vec ? dispatch_stream<T, true, OUT>(a, st) : dispatch_stream<T, false, OUT>(a, st);
   return launch_status(e);
 }
 
@@ -143,7 +146,7 @@ int check_shape(int64_t B, int64_t C, int64_t ld) {
   return FWB_OK;
 }
 
-RowArgs base_args(const float* z, const int64_t* y, int64_t B, int64_t C, int64_t ld,
+RowArgs base_args(const void* z, const int64_t* y, int64_t B, int64_t C, int64_t ld,
                   float* H, float* loss, int32_t* kappa, int32_t* status) {
   RowArgs a = {};
   a.z = z;
@@ -182,6 +185,7 @@ const char* fw_error_string(int code) {
     case FWB_E_POINTER: return "a required pointer is NULL";
     case FWB_E_LAUNCH: return "CUDA kernel launch failed";
     case FWB_E_CAPACITY: return "size exceeds the stated maximum";
+    case FWB_E_DTYPE: return "unsupported element type code";
     default: return "unknown error";
   }
 }
@@ -195,7 +199,24 @@ int fw_fused_fwd_bwd(const float* z, const int64_t* y, int64_t B, int64_t C, int
   a.scale = grad_scale;
   a.grad = grad;
   const bool vec = aligned16(z) && aligned16(grad) && (ld % 4 == 0);
-  return run_rows<kOutGrad>(a, static_cast<cudaStream_t>(stream), vec);
+  return run_rows<float, kOutGrad>(a, static_cast<cudaStream_t>(stream), vec);
+}
+
+int fw_fused_fwd_bwd_typed(int dtype, const void* z, const int64_t* y, int64_t B, int64_t C,
+                           int64_t ld, float grad_scale, void* grad, float* H, float* loss,
+                           int32_t* kappa, int32_t* status, void* stream) {
+  if (dtype != FWB_DTYPE_F32 && dtype != FWB_DTYPE_BF16 && dtype != FWB_DTYPE_F16) return FWB_E_DTYPE;
+  if (int rc = check_shape(B, C, ld)) return rc;
+  if (B > 0 && (!z || !y || !grad)) return FWB_E_POINTER;
+  RowArgs a = base_args(z, y, B, C, ld, H, loss, kappa, status);
+  a.scale = grad_scale;
+  a.grad = grad;
+  const int64_t eps = dtype == FWB_DTYPE_F32 ? 4 : 8;
+  const bool vec = aligned16(z) && aligned16(grad) && (ld % eps == 0);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == FWB_DTYPE_BF16) return run_rows<__nv_bfloat16, kOutGrad>(a, st, vec);
+  if (dtype == FWB_DTYPE_F16) return run_rows<__half, kOutGrad>(a, st, vec);
+  return run_rows<float, kOutGrad>(a, st, vec);
 }
 
 int fw_forward_mask(const float* z, const int64_t* y, int64_t B, int64_t C, int64_t ld,
@@ -207,7 +228,7 @@ int fw_forward_mask(const float* z, const int64_t* y, int64_t B, int64_t C, int6
   a.mask = mask;
   a.mask_vec = (C % 4 == 0) && ((reinterpret_cast<uintptr_t>(mask) & 3u) == 0);
   const bool vec = aligned16(z) && (ld % 4 == 0);
-  return run_rows<kOutMask>(a, static_cast<cudaStream_t>(stream), vec);
+  return run_rows<float, kOutMask>(a, static_cast<cudaStream_t>(stream), vec);
 }
 
 int fw_backward_mask(const int64_t* y, const uint8_t* mask, const int32_t* kappa, int64_t B,
@@ -233,7 +254,7 @@ int fw_forward_candidates(const float* z, const int64_t* y, int64_t B, int64_t C
   a.cand_idx = cand_idx;
   a.cand_count = cand_count;
   const bool vec = aligned16(z) && (ld % 4 == 0);
-  return run_rows<kOutCand>(a, static_cast<cudaStream_t>(stream), vec);
+  return run_rows<float, kOutCand>(a, static_cast<cudaStream_t>(stream), vec);
 }
 
 int fw_backward_candidates(const float* cand_val, const int32_t* cand_idx,
@@ -251,13 +272,31 @@ int fw_backward_candidates(const float* cand_val, const int32_t* cand_idx,
 
 int fw_scale_grad(float* grad, const float* grad_output, int per_row, float assumed_scale,
                   int64_t B, int64_t C, int64_t ld, void* stream) {
+  return fw_scale_grad_typed(FWB_DTYPE_F32, grad, grad_output, per_row, assumed_scale, B, C, ld,
+                             stream);
+}
+
+int fw_scale_grad_typed(int dtype, void* grad, const float* grad_output, int per_row,
+                        float assumed_scale, int64_t B, int64_t C, int64_t ld, void* stream) {
+  if (dtype != FWB_DTYPE_F32 && dtype != FWB_DTYPE_BF16 && dtype != FWB_DTYPE_F16) return FWB_E_DTYPE;
   if (int rc = check_shape(B, C, ld)) return rc;
   if (B == 0) return FWB_OK;
   if (!grad || !grad_output) return FWB_E_POINTER;
-  const int vec = aligned16(grad) && (ld % 4 == 0);
-  return launch_status(launch(fw_scale_grad_kernel, dim3(aux_grid(B, 1)), dim3(kAuxThreads), 1,
-                              static_cast<cudaStream_t>(stream), grad, grad_output, per_row,
-                              assumed_scale, B, C, ld, vec));
+  const int64_t eps = dtype == FWB_DTYPE_F32 ? 4 : 8;
+  const int vec = aligned16(grad) && (ld % eps == 0);
+  const dim3 grid(aux_grid(B, 1)), block(kAuxThreads);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (dtype == FWB_DTYPE_BF16)
+    e = launch(fw_scale_grad_kernel<__nv_bfloat16>, grid, block, 1, st,
+               static_cast<__nv_bfloat16*>(grad), grad_output, per_row, assumed_scale, B, C, ld, vec);
+  else if (dtype == FWB_DTYPE_F16)
+    e = launch(fw_scale_grad_kernel<__half>, grid, block, 1, st, static_cast<__half*>(grad),
+               grad_output, per_row, assumed_scale, B, C, ld, vec);
+  else
+    e = launch(fw_scale_grad_kernel<float>, grid, block, 1, st, static_cast<float*>(grad),
+               grad_output, per_row, assumed_scale, B, C, ld, vec);
+  return launch_status(e);
 }
 
 int fw_loss_reduce(const float* loss, int64_t B, double scale, float* out, void* stream) {

@@ -14,6 +14,8 @@
 //           S_k - 1 would lose the 1 entirely.
 #pragma once
 
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <math_constants.h>
 #include <stdint.h>
@@ -26,14 +28,88 @@ constexpr unsigned kFull = 0xffffffffu;
 // support as a (value, column) list.
 enum OutMode : int { kOutGrad = 0, kOutMask = 1, kOutCand = 2 };
 
+// Element types of logits and gradient.  Arithmetic is fp32/fp64 for all of
+// them; a 16-byte slot holds kEPS elements.
+template <class T> struct Elem;
+template <> struct Elem<float> {
+  static constexpr int kEPS = 4;
+  __device__ static float to_f(float x) { return x; }
+  __device__ static float from_f(float x) { return x; }
+};
+template <> struct Elem<__nv_bfloat16> {
+  static constexpr int kEPS = 8;
+  __device__ static float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+  __device__ static __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
+  __device__ static float bits_to_f(uint32_t b) { return __uint_as_float(b << 16); }
+  __device__ static uint32_t f_to_bits(float x) { return __bfloat16_as_ushort(__float2bfloat16_rn(x)); }
+};
+template <> struct Elem<__half> {
+  static constexpr int kEPS = 8;
+  __device__ static float to_f(__half x) { return __half2float(x); }
+  __device__ static __half from_f(float x) { return __float2half_rn(x); }
+  __device__ static float bits_to_f(uint32_t b) { return __half2float(__ushort_as_half((unsigned short)b)); }
+  __device__ static uint32_t f_to_bits(float x) { return __half_as_ushort(__float2half_rn(x)); }
+};
+
+// 16-byte slot <-> kEPS floats.
+template <class T>
+__device__ __forceinline__ void unpack16(const uint4& u, float* out) {
+  if constexpr (sizeof(T) == 4) {
+    out[0] = __uint_as_float(u.x);
+    out[1] = __uint_as_float(u.y);
+    out[2] = __uint_as_float(u.z);
+    out[3] = __uint_as_float(u.w);
+  } else {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      out[2 * k] = Elem<T>::bits_to_f(w[k] & 0xffffu);
+      out[2 * k + 1] = Elem<T>::bits_to_f(w[k] >> 16);
+    }
+  }
+}
+
+template <class T>
+__device__ __forceinline__ uint4 pack16(const float* in) {
+  if constexpr (sizeof(T) == 4) {
+    return make_uint4(__float_as_uint(in[0]), __float_as_uint(in[1]), __float_as_uint(in[2]),
+                      __float_as_uint(in[3]));
+  } else {
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      w[k] = Elem<T>::f_to_bits(in[2 * k]) | (Elem<T>::f_to_bits(in[2 * k + 1]) << 16);
+    return make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// Streaming 16-byte load that does not pollute L1.
+__device__ __forceinline__ uint4 ld_stream16(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+template <class T>
+__device__ __forceinline__ float ld_elem(const T* p) {
+  return Elem<T>::to_f(*p);
+}
+
+template <class T>
+__device__ __forceinline__ void st_elem(T* p, float v) {
+  *p = Elem<T>::from_f(v);
+}
+
 struct RowArgs {
-  const float* z;        // [B, ld]
+  const void* z;         // [B, ld] of the element type
   const int64_t* y;      // [B]
   int64_t B;
   int64_t C;
   int64_t ld;
   float scale;           // gradient scale (1/B for "mean")
-  float* grad;           // kOutGrad: [B, ld]
+  void* grad;            // kOutGrad: [B, ld] of the element type
   uint8_t* mask;         // kOutMask: [B, C]
   float* cand_val;       // kOutCand: [B, C]
   int32_t* cand_idx;     // kOutCand: [B, C]

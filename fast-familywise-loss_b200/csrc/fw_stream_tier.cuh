@@ -53,7 +53,7 @@ constexpr int kST = 256;              // threads per CTA
 constexpr int kSW = kST / 32;         // warps per CTA
 constexpr int kStreamListCap = 128;   // candidates per warp list
 constexpr int kSolveCap = 1024;       // gathered candidates per row
-constexpr int kStreamU = 4;           // 16-byte items per thread per step
+constexpr int kStreamValues = 16;     // values per thread per streaming step
 
 struct __align__(16) StreamShared {
   float lz[kSW][kStreamListCap];
@@ -153,15 +153,15 @@ __device__ __forceinline__ void list_append(float* lz, int* li, int& cnt,
 }
 
 // Segment of the row owned by one CTA: items [i0, i1) where an item is a
-// float4 (VEC) or a float.  With VEC, the C % 4 tail columns belong to the
-// last CTA and are handled by its warp 0.
+// 16-byte slot of EPS elements (VEC) or one element.  With VEC, the C % EPS
+// tail columns belong to the last CTA and are handled by its warp 0.
 struct Segment {
   int64_t i0, i1;
 };
 
-template <int CS, bool VEC>
+template <int CS, bool VEC, int EPS>
 __device__ __forceinline__ Segment row_segment(int64_t C, int rank) {
-  const int64_t n = VEC ? C / 4 : C;
+  const int64_t n = VEC ? C / EPS : C;
   Segment g;
   g.i0 = n * rank / CS;
   g.i1 = n * (rank + 1) / CS;
@@ -171,26 +171,27 @@ __device__ __forceinline__ Segment row_segment(int64_t C, int rank) {
 // Calls f(value, column) for every element of this thread's share of the
 // segment, in the fixed order used by all passes (loads are issued kStreamU
 // 16-byte items ahead).  f must be thread-local work only.
-template <int CS, bool VEC, class F>
-__device__ __forceinline__ void for_each_element(const float* zr, int64_t C,
+template <class T, int CS, bool VEC, class F>
+__device__ __forceinline__ void for_each_element(const T* zr, int64_t C,
                                                  int rank, F&& f) {
-  const Segment g = row_segment<CS, VEC>(C, rank);
-  constexpr int W = VEC ? 4 : 1;
-  constexpr int IPT = VEC ? kStreamU : kStreamU * 4;
+  constexpr int EPS = Elem<T>::kEPS;
+  const Segment g = row_segment<CS, VEC, EPS>(C, rank);
+  constexpr int W = VEC ? EPS : 1;
+  constexpr int IPT = kStreamValues / W;
   for (int64_t base = g.i0; base < g.i1; base += (int64_t)kST * IPT) {
     float v[IPT * W];
 #pragma unroll
     for (int u = 0; u < IPT; ++u) {
       const int64_t it = base + (int64_t)u * kST + threadIdx.x;
       if (VEC) {
-        float4 q = make_float4(-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F);
-        if (it < g.i1) q = ld_stream4(zr + 4 * it);
-        v[4 * u + 0] = q.x;
-        v[4 * u + 1] = q.y;
-        v[4 * u + 2] = q.z;
-        v[4 * u + 3] = q.w;
+        if (it < g.i1) {
+          unpack16<T>(ld_stream16(zr + W * it), &v[W * u]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < W; ++j) v[W * u + j] = -CUDART_INF_F;
+        }
       } else {
-        v[u] = (it < g.i1) ? ld_stream1(zr + it) : -CUDART_INF_F;
+        v[u] = (it < g.i1) ? ld_elem(zr + it) : -CUDART_INF_F;
       }
     }
 #pragma unroll
@@ -203,14 +204,16 @@ __device__ __forceinline__ void for_each_element(const float* zr, int64_t C,
     }
   }
   if (VEC && rank == CS - 1 && threadIdx.x < 32) {
-    const int64_t c = 4 * (C / 4) + threadIdx.x;
-    if (c < C) f(zr[c], (int)c);
+    const int64_t c = EPS * (C / EPS) + threadIdx.x;
+    if (c < C) f(ld_elem(zr + c), (int)c);
   }
 }
 
-template <int CS, bool VEC, int OUT>
+template <class T, int CS, bool VEC, int OUT>
 __global__ void __launch_bounds__(kST)
     fw_stream_rows_kernel(RowArgs a) {
+  static_assert(OUT == kOutGrad || sizeof(T) == 4, "mask/candidate outputs are fp32-only");
+  constexpr int EPS = Elem<T>::kEPS;
   __shared__ StreamShared s;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -220,7 +223,7 @@ __global__ void __launch_bounds__(kST)
   if constexpr (CS > 1) rank = (int)cooperative_groups::this_cluster().block_rank();
   const bool leader = (rank == 0);
   const int64_t C = a.C;
-  const float* zr = a.z + row * a.ld;
+  const T* zr = static_cast<const T*>(a.z) + row * a.ld;
 
   if (tid == 0) {
     s.run_key = 0u;
@@ -232,15 +235,15 @@ __global__ void __launch_bounds__(kST)
   __syncthreads();
 
   // ---------------------------------------------------------------- stream
-  constexpr int W = VEC ? 4 : 1;
-  constexpr int IPT = VEC ? kStreamU : kStreamU * 4;
-  const Segment g = row_segment<CS, VEC>(C, rank);
+  constexpr int W = VEC ? EPS : 1;
+  constexpr int IPT = kStreamValues / W;
+  const Segment g = row_segment<CS, VEC, EPS>(C, rank);
   float run = -CUDART_INF_F;
   int wcnt = 0;
   bool ovf = false;
   float* lz = s.lz[w];
   int* li = s.li[w];
-  float* gr = (OUT == kOutGrad) ? a.grad + row * a.ld : nullptr;
+  T* gr = (OUT == kOutGrad) ? static_cast<T*>(a.grad) + row * a.ld : nullptr;
   uint8_t* mr = (OUT == kOutMask) ? a.mask + row * C : nullptr;
 
   for (int64_t base = g.i0; base < g.i1; base += (int64_t)kST * IPT) {
@@ -249,14 +252,14 @@ __global__ void __launch_bounds__(kST)
     for (int u = 0; u < IPT; ++u) {
       const int64_t it = base + (int64_t)u * kST + tid;
       if (VEC) {
-        float4 q = make_float4(-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F);
-        if (it < g.i1) q = ld_stream4(zr + 4 * it);
-        v[4 * u + 0] = q.x;
-        v[4 * u + 1] = q.y;
-        v[4 * u + 2] = q.z;
-        v[4 * u + 3] = q.w;
+        if (it < g.i1) {
+          unpack16<T>(ld_stream16(zr + W * it), &v[W * u]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < W; ++j) v[W * u + j] = -CUDART_INF_F;
+        }
       } else {
-        v[u] = (it < g.i1) ? ld_stream1(zr + it) : -CUDART_INF_F;
+        v[u] = (it < g.i1) ? ld_elem(zr + it) : -CUDART_INF_F;
       }
     }
 #pragma unroll
@@ -265,9 +268,9 @@ __global__ void __launch_bounds__(kST)
       if (it < g.i1) {
         if (OUT == kOutGrad) {
           if (VEC)
-            *reinterpret_cast<float4*>(gr + 4 * it) = make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<uint4*>(gr + W * it) = make_uint4(0u, 0u, 0u, 0u);
           else
-            gr[it] = 0.0f;
+            st_elem(gr + it, 0.0f);
         } else if (OUT == kOutMask) {
           if (VEC && a.mask_vec)
             *reinterpret_cast<uchar4*>(mr + 4 * it) = make_uchar4(0, 0, 0, 0);
@@ -300,12 +303,12 @@ __global__ void __launch_bounds__(kST)
     }
   }
   if (VEC && rank == CS - 1 && w == 0) {
-    // C % 4 tail columns.
-    const int64_t c = 4 * (C / 4) + lane;
+    // C % EPS tail columns.
+    const int64_t c = EPS * (C / EPS) + lane;
     const bool in = c < C;
-    const float x = in ? zr[c] : -CUDART_INF_F;
+    const float x = in ? ld_elem(zr + c) : -CUDART_INF_F;
     if (in) {
-      if (OUT == kOutGrad) gr[c] = 0.0f;
+      if (OUT == kOutGrad) st_elem(gr + c, 0.0f);
       if (OUT == kOutMask) mr[c] = 0;
     }
     run = max_nan(run, warp_max_nan(x));
@@ -351,7 +354,7 @@ __global__ void __launch_bounds__(kST)
   if (!isfinite(M)) {
     const bool isn = (M != M);
     int best = INT_MAX;
-    for_each_element<CS, VEC>(zr, C, rank, [&](float x, int c) {
+    for_each_element<T, CS, VEC>(zr, C, rank, [&](float x, int c) {
       if (isn ? (x != x) : (x == M)) best = min(best, c);
     });
     best = (int)__reduce_min_sync(kFull, (unsigned)best);
@@ -365,14 +368,14 @@ __global__ void __launch_bounds__(kST)
     row_barrier<CS>();
     if (!(leader && tid == 0)) return;
     const int j = s.nsolve;
-    const float zy = yok ? zr[yc] : CUDART_NAN_F;
+    const float zy = yok ? ld_elem(zr + yc) : CUDART_NAN_F;
     if (OUT == kOutGrad) {
-      gr[j] = a.scale - ((j == yc) ? a.scale : 0.0f);
-      if (yok && j != yc) gr[yc] = -a.scale;
+      st_elem(gr + j, a.scale - ((j == yc) ? a.scale : 0.0f));
+      if (yok && j != yc) st_elem(gr + yc, -a.scale);
     } else if (OUT == kOutMask) {
       mr[j] = 1;
     } else {
-      a.cand_val[row * C] = zr[j];
+      a.cand_val[row * C] = ld_elem(zr + j);
       a.cand_idx[row * C] = j;
       if (a.cand_count) a.cand_count[row] = 1;
     }
@@ -442,11 +445,11 @@ __global__ void __launch_bounds__(kST)
             gv -= a.scale;
             ysel = true;
           }
-          gr[col] = gv;
+          st_elem(gr + col, gv);
         }
       }
       ysel = __any_sync(kFull, ysel);
-      if (lane == 0 && yok && !ysel) gr[yc] = -a.scale;
+      if (lane == 0 && yok && !ysel) st_elem(gr + yc, -a.scale);
     } else if (OUT == kOutMask) {
       for (int k = lane; k < n; k += 32)
         if (s.sz[k] > Hf) mr[s.si[k]] = 1;
@@ -468,7 +471,7 @@ __global__ void __launch_bounds__(kST)
       if (lane == 0 && a.cand_count) a.cand_count[row] = kap;
     }
     if (lane == 0) {
-      const float zy = yok ? zr[yc] : CUDART_NAN_F;
+      const float zy = yok ? ld_elem(zr + yc) : CUDART_NAN_F;
       if (a.H) a.H[row] = Hf;
       if (a.loss) a.loss[row] = yok ? row_loss(M, tau, zy) : CUDART_NAN_F;
       if (a.kappa) a.kappa[row] = kap;
@@ -489,7 +492,7 @@ __global__ void __launch_bounds__(kST)
       s.hs[b] = 0.0;
     }
     __syncthreads();
-    for_each_element<CS, VEC>(zr, C, rank, [&](float x, int) {
+    for_each_element<T, CS, VEC>(zr, C, rank, [&](float x, int) {
       if (x > t0) {
         const uint32_t k = sort_key(x);
         if ((k & pmask) == prefix) {
@@ -573,18 +576,18 @@ __global__ void __launch_bounds__(kST)
     return x > t0 && (unsigned long long)sort_key(x) >= cut;
   };
   if (OUT == kOutGrad) {
-    for_each_element<CS, VEC>(zr, C, rank, [&](float x, int c) {
+    for_each_element<T, CS, VEC>(zr, C, rank, [&](float x, int c) {
       float gv = sel_of(x) ? inv : 0.0f;
       if (c == yc) gv -= a.scale;
-      gr[c] = gv;
+      st_elem(gr + c, gv);
     });
   } else if (OUT == kOutMask) {
-    for_each_element<CS, VEC>(zr, C, rank, [&](float x, int c) { mr[c] = sel_of(x) ? 1 : 0; });
+    for_each_element<T, CS, VEC>(zr, C, rank, [&](float x, int c) { mr[c] = sel_of(x) ? 1 : 0; });
   } else {
     int* pos_ctr = &cta_smem<CS>(&s, 0)->cand_pos;
     float* cv = a.cand_val + row * C;
     int32_t* ci = a.cand_idx + row * C;
-    for_each_element<CS, VEC>(zr, C, rank, [&](float x, int c) {
+    for_each_element<T, CS, VEC>(zr, C, rank, [&](float x, int c) {
       if (sel_of(x)) {
         const int p = atomicAdd(pos_ctr, 1);
         cv[p] = x;
@@ -594,7 +597,7 @@ __global__ void __launch_bounds__(kST)
   }
   row_barrier<CS>();
   if (leader && tid == 0) {
-    const float zy = yok ? zr[yc] : CUDART_NAN_F;
+    const float zy = yok ? ld_elem(zr + yc) : CUDART_NAN_F;
     if (a.H) a.H[row] = threshold_fp32(M, tau);
     if (a.loss) a.loss[row] = yok ? row_loss(M, tau, zy) : CUDART_NAN_F;
     if (a.kappa) a.kappa[row] = kap;

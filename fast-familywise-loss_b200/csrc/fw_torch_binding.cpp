@@ -30,11 +30,25 @@ void check_rc(int rc, const char* what) {
   TORCH_CHECK(rc == FWB_OK, what, " failed: ", fw_error_string(rc));
 }
 
-void check_logits(const torch::Tensor& logits) {
+void check_logits(const torch::Tensor& logits, bool any_float = false) {
   TORCH_CHECK(logits.is_cuda(), "logits must be a CUDA tensor");
   TORCH_CHECK(logits.dim() == 2, "logits must have shape [N, K]");
-  TORCH_CHECK(logits.scalar_type() == torch::kFloat32, "logits must be float32");
+  if (any_float) {
+    TORCH_CHECK(logits.scalar_type() == torch::kFloat32 || logits.scalar_type() == torch::kBFloat16 ||
+                    logits.scalar_type() == torch::kHalf,
+                "logits must be float32, bfloat16 or float16");
+  } else {
+    TORCH_CHECK(logits.scalar_type() == torch::kFloat32, "logits must be float32");
+  }
   TORCH_CHECK(logits.size(1) >= 1, "logits must have K >= 1 columns");
+}
+
+int dtype_code(const torch::Tensor& t) {
+  switch (t.scalar_type()) {
+    case torch::kBFloat16: return FWB_DTYPE_BF16;
+    case torch::kHalf: return FWB_DTYPE_F16;
+    default: return FWB_DTYPE_F32;
+  }
 }
 
 void check_targets(const torch::Tensor& targets, int64_t N, const torch::Tensor& like) {
@@ -173,10 +187,11 @@ torch::Tensor fw_backward(torch::Tensor logits, torch::Tensor targets, torch::Te
 }
 
 // Fused forward + backward (new): (grad, H, losses, kappa), grad scaled by
-// grad_scale; `status` is an optional int32 [1] device word.
+// grad_scale and of the logits' dtype (float32, bfloat16 or float16), H and
+// losses float32; `status` is an optional int32 [1] device word.
 std::vector<torch::Tensor> fused_fwd_bwd(torch::Tensor logits, torch::Tensor targets,
                                          double grad_scale, c10::optional<torch::Tensor> status) {
-  check_logits(logits);
+  check_logits(logits, true);
   const c10::cuda::CUDAGuard guard(logits.device());
   const int64_t N = logits.size(0), K = logits.size(1);
   check_targets(targets, N, logits);
@@ -185,8 +200,8 @@ std::vector<torch::Tensor> fused_fwd_bwd(torch::Tensor logits, torch::Tensor tar
   auto y = targets.contiguous();
   auto grad = (ld == K) ? torch::empty({N, K}, logits.options())
                         : torch::empty_strided({N, K}, {ld, 1}, logits.options());
-  auto H = torch::empty({N}, logits.options());
-  auto losses = torch::empty({N}, logits.options());
+  auto H = torch::empty({N}, logits.options().dtype(torch::kFloat32));
+  auto losses = torch::empty({N}, logits.options().dtype(torch::kFloat32));
   auto kappa = torch::empty({N}, i32(logits));
   int32_t* st = nullptr;
   if (status.has_value()) {
@@ -194,24 +209,25 @@ std::vector<torch::Tensor> fused_fwd_bwd(torch::Tensor logits, torch::Tensor tar
                 "status must be an int32 CUDA tensor");
     st = status->data_ptr<int32_t>();
   }
-  check_rc(fw_fused_fwd_bwd(z.data_ptr<float>(), y.data_ptr<int64_t>(), N, K, ld, (float)grad_scale,
-                            grad.data_ptr<float>(), H.data_ptr<float>(), losses.data_ptr<float>(),
-                            kappa.data_ptr<int32_t>(), st, cur_stream()),
+  check_rc(fw_fused_fwd_bwd_typed(dtype_code(z), z.data_ptr(), y.data_ptr<int64_t>(), N, K, ld,
+                                  (float)grad_scale, grad.data_ptr(), H.data_ptr<float>(),
+                                  losses.data_ptr<float>(), kappa.data_ptr<int32_t>(), st, cur_stream()),
            "fw_fused_fwd_bwd");
   return {grad, H, losses, kappa};
 }
 
 // grad (in place) *= grad_output[per_row ? r : 0] / assumed_scale.
 void scale_grad(torch::Tensor grad, torch::Tensor grad_output, bool per_row, double assumed_scale) {
-  TORCH_CHECK(grad.is_cuda() && grad.dim() == 2 && grad.scalar_type() == torch::kFloat32 &&
-                  grad.stride(1) == 1,
-              "grad must be a row-major float32 CUDA matrix");
+  TORCH_CHECK(grad.is_cuda() && grad.dim() == 2 && grad.stride(1) == 1 &&
+                  (grad.scalar_type() == torch::kFloat32 || grad.scalar_type() == torch::kBFloat16 ||
+                   grad.scalar_type() == torch::kHalf),
+              "grad must be a row-major float32/bfloat16/float16 CUDA matrix");
   const c10::cuda::CUDAGuard guard(grad.device());
   auto go = grad_output.to(grad.device(), torch::kFloat32).contiguous();
   TORCH_CHECK(go.numel() >= (per_row ? grad.size(0) : 1), "grad_output too small");
   const int64_t ld = grad.size(0) > 1 ? grad.stride(0) : grad.size(1);
-  check_rc(fw_scale_grad(grad.data_ptr<float>(), go.data_ptr<float>(), per_row ? 1 : 0,
-                         (float)assumed_scale, grad.size(0), grad.size(1), ld, cur_stream()),
+  check_rc(fw_scale_grad_typed(dtype_code(grad), grad.data_ptr(), go.data_ptr<float>(), per_row ? 1 : 0,
+                               (float)assumed_scale, grad.size(0), grad.size(1), ld, cur_stream()),
            "fw_scale_grad");
 }
 

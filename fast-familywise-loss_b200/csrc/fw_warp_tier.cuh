@@ -1,13 +1,15 @@
 // Register tier (C <= 2048): a group of G lanes (G = 8, 16 or 32; 32/G rows
 // per warp) holds one row in registers, so the row is read from HBM once and
 // its output written once, with no shared-memory traffic except the short
-// candidate list.
+// candidate list.  Element type T = float, bf16 or fp16 (arithmetic in
+// fp32/fp64); a lane owns NS 16-byte slots of EPS elements.
 //
 // Per row:
-//   1. load (128-bit when rows are 16-byte aligned), M = NaN-propagating max
-//      by xor shuffles inside the group;
-//   2. candidates z > t0 are compacted into a per-group list by an exclusive
-//      shuffle scan (the common case: a handful of elements);
+//   1. load (16-byte loads when rows are 16-byte aligned), M = NaN-propagating
+//      max by xor shuffles inside the group;
+//   2. n = |{z > t0}|; a unique maximum (n == 1) is solved on the spot
+//      (kappa = 1, h* = M - 1); otherwise the candidates are compacted into a
+//      per-group list by an exclusive shuffle scan;
 //   3. exact threshold: Michelot's fixed point on the list (michelot_list),
 //      or on the registers when the list would overflow (near-constant rows
 //      where most of the row is within 1 of the max);
@@ -33,48 +35,50 @@ constexpr int kWarpTierThreads = 256;
 constexpr int kWarpTierWarps = kWarpTierThreads / 32;
 constexpr int kWarpListCap = 128;  // list entries per warp, split between its groups
 
-// Column of register slot (i, j) of lane `li` of a G-lane group.  Aligned rows
-// use 128-bit loads (a lane owns 4 consecutive columns per slot); unaligned
-// rows use lane-contiguous scalar loads so every load instruction coalesces.
-template <int G, bool VEC>
+// Column of register value (i, j) (slot i, element j) of lane `li` of a G-lane
+// group.  Aligned rows use 16-byte loads (a lane owns EPS consecutive columns
+// per slot); unaligned rows use lane-contiguous scalar loads so every load
+// instruction coalesces.
+template <int G, int EPS, bool VEC>
 __device__ __forceinline__ int group_slot_col(int i, int j, int li) {
-  return VEC ? ((i * G + li) * 4 + j) : ((i * 4 + j) * G + li);
+  return VEC ? ((i * G + li) * EPS + j) : ((i * EPS + j) * G + li);
 }
 
-// Stores the 4 values of register slot i (columns group_slot_col(i, 0..3)).
-template <int G, bool VEC, bool FULL4 = false>
-__device__ __forceinline__ void warp_tier_store4(float* gr, int i, int li, int C, const float (&g)[4]) {
-  if (VEC && FULL4) {
-    const int c0 = (i * G + li) * 4;
-    if (c0 < C) *reinterpret_cast<float4*>(gr + c0) = make_float4(g[0], g[1], g[2], g[3]);
-  } else if (VEC) {
-    const int c0 = (i * G + li) * 4;
-    if (c0 + 3 < C) {
-      *reinterpret_cast<float4*>(gr + c0) = make_float4(g[0], g[1], g[2], g[3]);
+// Stores the EPS values of slot i.  FULLV: C % EPS == 0 (a slot is entirely
+// inside or outside the row).
+template <class T, int G, bool VEC, bool FULLV>
+__device__ __forceinline__ void warp_tier_store_slot(T* gr, int i, int li, int C, const float* g) {
+  constexpr int EPS = Elem<T>::kEPS;
+  if (VEC) {
+    const int c0 = (i * G + li) * EPS;
+    if (FULLV || c0 + EPS - 1 < C) {
+      if (FULLV && c0 >= C) return;
+      *reinterpret_cast<uint4*>(gr + c0) = pack16<T>(g);
     } else {
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if (c0 + j < C) gr[c0 + j] = g[j];
+      for (int j = 0; j < EPS; ++j)
+        if (c0 + j < C) st_elem(gr + c0 + j, g[j]);
     }
   } else {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int c = group_slot_col<G, false>(i, j, li);
-      if (c < C) gr[c] = g[j];
+    for (int j = 0; j < EPS; ++j) {
+      const int c = group_slot_col<G, EPS, false>(i, j, li);
+      if (c < C) st_elem(gr + c, g[j]);
     }
   }
 }
 
-template <int G, bool VEC, bool FULL4 = false>
-__device__ __forceinline__ void warp_tier_store4_mask(uint8_t* mr, int i, int li, int C, int mask_vec,
-                                                      const uint8_t (&b)[4]) {
+template <int G, bool VEC, bool FULLV>
+__device__ __forceinline__ void warp_tier_store_mask(uint8_t* mr, int i, int li, int C, int mask_vec,
+                                                     const uint8_t (&b)[4]) {
   const int c0 = (i * G + li) * 4;
-  if (VEC && mask_vec && c0 + 3 < C) {
+  if (VEC && mask_vec && (FULLV || c0 + 3 < C)) {
+    if (FULLV && c0 >= C) return;
     *reinterpret_cast<uchar4*>(mr + c0) = make_uchar4(b[0], b[1], b[2], b[3]);
   } else {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int c = group_slot_col<G, VEC>(i, j, li);
+      const int c = group_slot_col<G, 4, VEC>(i, j, li);
       if (c < C) mr[c] = b[j];
     }
   }
@@ -82,45 +86,48 @@ __device__ __forceinline__ void warp_tier_store4_mask(uint8_t* mr, int i, int li
 
 // Row whose maximum is NaN or +-inf: kappa = 1 at the first column holding
 // the maximum (the first NaN for NaN rows), H = M, loss = 1 - z_y + M (fp32).
-template <int G, int NS4, bool VEC, int OUT>
-__device__ __forceinline__ void warp_tier_nonfinite(const RowArgs& a, int64_t row, const float (&v)[NS4 * 4],
-                                                 float m, int li, unsigned gmask, int yc, float zy) {
+template <class T, int G, int NS, bool VEC, int OUT>
+__device__ __forceinline__ void warp_tier_nonfinite(const RowArgs& a, int64_t row,
+                                                    const float (&v)[NS * Elem<T>::kEPS], float m,
+                                                    int li, unsigned gmask, int yc, float zy) {
+  constexpr int EPS = Elem<T>::kEPS;
   const int C = (int)a.C;
   const bool isn = (m != m);
   unsigned best = 0xffffffffu;
 #pragma unroll
-  for (int i = 0; i < NS4; ++i)
+  for (int i = 0; i < NS; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int c = group_slot_col<G, VEC>(i, j, li);
-      const float x = v[4 * i + j];
+    for (int j = 0; j < EPS; ++j) {
+      const int c = group_slot_col<G, EPS, VEC>(i, j, li);
+      const float x = v[EPS * i + j];
       if (c < C && (isn ? (x != x) : (x == m))) best = min(best, (unsigned)c);
     }
   const int jstar = (int)group_min<G>(best, gmask);
   if (OUT == kOutGrad) {
-    float* gr = a.grad + row * a.ld;
+    T* gr = static_cast<T*>(a.grad) + row * a.ld;
 #pragma unroll
-    for (int i = 0; i < NS4; ++i) {
-      float g[4];
+    for (int i = 0; i < NS; ++i) {
+      float g[EPS];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) g[j] = (group_slot_col<G, VEC>(i, j, li) == jstar) ? a.scale : 0.0f;
-      warp_tier_store4<G, VEC>(gr, i, li, C, g);
+      for (int j = 0; j < EPS; ++j)
+        g[j] = (group_slot_col<G, EPS, VEC>(i, j, li) == jstar) ? a.scale : 0.0f;
+      warp_tier_store_slot<T, G, VEC, false>(gr, i, li, C, g);
     }
     if (yc >= 0) {
       __syncwarp(gmask);
-      if (li == 0) gr[yc] = ((yc == jstar) ? a.scale : 0.0f) - a.scale;
+      if (li == 0) st_elem(gr + yc, ((yc == jstar) ? a.scale : 0.0f) - a.scale);
     }
   } else if (OUT == kOutMask) {
     uint8_t* mr = a.mask + row * a.C;
 #pragma unroll
-    for (int i = 0; i < NS4; ++i) {
+    for (int i = 0; i < NS; ++i) {
       uint8_t b[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) b[j] = (group_slot_col<G, VEC>(i, j, li) == jstar) ? 1 : 0;
-      warp_tier_store4_mask<G, VEC>(mr, i, li, C, a.mask_vec, b);
+      for (int j = 0; j < 4; ++j) b[j] = (group_slot_col<G, 4, VEC>(i, j, li) == jstar) ? 1 : 0;
+      warp_tier_store_mask<G, VEC, false>(mr, i, li, C, a.mask_vec, b);
     }
   } else if (li == 0) {
-    a.cand_val[row * a.C] = a.z[row * a.ld + jstar];
+    a.cand_val[row * a.C] = ld_elem(static_cast<const T*>(a.z) + row * a.ld + jstar);
     a.cand_idx[row * a.C] = jstar;
     if (a.cand_count) a.cand_count[row] = 1;
   }
@@ -133,21 +140,21 @@ __device__ __forceinline__ void warp_tier_nonfinite(const RowArgs& a, int64_t ro
   }
 }
 
-// Resident CTAs per SM the register budget is sized for (no spills): 3 (85
-// registers) up to 16 values per lane, 2 (128) at 32, 1 at 64.
-template <int NS4>
+// Resident CTAs per SM the register budget is sized for: 3 (85 registers) up
+// to 16 values per lane, 2 (128) at 32, 1 at 64.
+template <int NV>
 constexpr int warp_tier_min_blocks() {
-  return NS4 <= 4 ? 3 : (NS4 <= 8 ? 2 : 1);
+  return NV <= 16 ? 3 : (NV <= 32 ? 2 : 1);
 }
 
-// FULL4 (with VEC): C % 4 == 0, so every 16-byte slot is entirely inside or
-// entirely outside the row and loads/stores need one predicate per slot.
-template <int G, int NS4, bool VEC, int OUT, bool FULL4>
-__global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS4>())
+template <class T, int G, int NS, bool VEC, int OUT, bool FULLV>
+__global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS * Elem<T>::kEPS>())
     fw_warp_rows_kernel(RowArgs a) {
-  constexpr int NS = NS4 * 4;           // register slots per lane
+  constexpr int EPS = Elem<T>::kEPS;
+  constexpr int NV = NS * EPS;          // register values per lane
   constexpr int RPW = 32 / G;           // rows per warp
   constexpr int CAPG = kWarpListCap / RPW;
+  static_assert(OUT == kOutGrad || sizeof(T) == 4, "mask/candidate outputs are fp32-only");
   __shared__ float s_list[kWarpTierWarps][kWarpListCap];
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
@@ -157,62 +164,58 @@ __global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS4>())
   float* L = &s_list[wib][gi * CAPG];
   const int C = (int)a.C;
   const int64_t ngroups = (int64_t)gridDim.x * kWarpTierWarps * RPW;
+  const T* zbase = static_cast<const T*>(a.z);
 
   for (int64_t row = ((int64_t)blockIdx.x * kWarpTierWarps + wib) * RPW + gi; row < a.B;
        row += ngroups) {
-    const float* zr = a.z + row * a.ld;
+    const T* zr = zbase + row * a.ld;
     const int64_t ylab = a.y[row];
-    float v[NS];
+    float v[NV];
 #pragma unroll
-    for (int i = 0; i < NS4; ++i) {
-      if (VEC && FULL4) {
-        const int c0 = (i * G + li) * 4;
-        float4 q = make_float4(-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F);
-        if (c0 < C) q = ld_stream4(zr + c0);
-        v[4 * i + 0] = q.x;
-        v[4 * i + 1] = q.y;
-        v[4 * i + 2] = q.z;
-        v[4 * i + 3] = q.w;
-      } else if (VEC) {
-        const int c0 = (i * G + li) * 4;
-        if (c0 + 3 < C) {
-          const float4 q = ld_stream4(zr + c0);
-          v[4 * i + 0] = q.x;
-          v[4 * i + 1] = q.y;
-          v[4 * i + 2] = q.z;
-          v[4 * i + 3] = q.w;
+    for (int i = 0; i < NS; ++i) {
+      if (VEC) {
+        const int c0 = (i * G + li) * EPS;
+        if (FULLV || c0 + EPS - 1 < C) {
+          uint4 u = make_uint4(0u, 0u, 0u, 0u);
+          const bool in = !FULLV || c0 < C;
+          if (in) u = ld_stream16(zr + c0);
+          unpack16<T>(u, &v[EPS * i]);
+          if (!in) {
+#pragma unroll
+            for (int j = 0; j < EPS; ++j) v[EPS * i + j] = -CUDART_INF_F;
+          }
         } else {
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            v[4 * i + j] = (c0 + j < C) ? ld_stream1(zr + c0 + j) : -CUDART_INF_F;
+          for (int j = 0; j < EPS; ++j)
+            v[EPS * i + j] = (c0 + j < C) ? ld_elem(zr + c0 + j) : -CUDART_INF_F;
         }
       } else {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int c = group_slot_col<G, false>(i, j, li);
-          v[4 * i + j] = (c < C) ? ld_stream1(zr + c) : -CUDART_INF_F;
+        for (int j = 0; j < EPS; ++j) {
+          const int c = group_slot_col<G, EPS, false>(i, j, li);
+          v[EPS * i + j] = (c < C) ? ld_elem(zr + c) : -CUDART_INF_F;
         }
       }
     }
 
     float m = -CUDART_INF_F;
 #pragma unroll
-    for (int s = 0; s < NS; ++s) m = max_nan(m, v[s]);
+    for (int s = 0; s < NV; ++s) m = max_nan(m, v[s]);
     m = group_max_nan<G>(m, gmask);
 
     const bool yok = (ylab >= 0 && ylab < a.C);
     const int yc = yok ? (int)ylab : -1;
-    const float zy = yok ? __ldg(zr + yc) : CUDART_NAN_F;
+    const float zy = yok ? ld_elem(zr + yc) : CUDART_NAN_F;
 
     if (!isfinite(m)) {  // group-uniform; rare
-      warp_tier_nonfinite<G, NS4, VEC, OUT>(a, row, v, m, li, gmask, yc, zy);
+      warp_tier_nonfinite<T, G, NS, VEC, OUT>(a, row, v, m, li, gmask, yc, zy);
       continue;
     }
 
     const float t0 = __fsub_rd(m, 1.0f);
     int c = 0;
 #pragma unroll
-    for (int s = 0; s < NS; ++s) c += (v[s] > t0) ? 1 : 0;
+    for (int s = 0; s < NV; ++s) c += (v[s] > t0) ? 1 : 0;
     const int n = group_sum<G>(c, gmask);
     double tau;
     int kap;
@@ -224,7 +227,7 @@ __global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS4>())
       int off = group_excl_scan<G>(c, li, gmask);
       if (c > 0) {
 #pragma unroll
-        for (int s = 0; s < NS; ++s)
+        for (int s = 0; s < NV; ++s)
           if (v[s] > t0) L[off++] = v[s];
       }
       __syncwarp(gmask);
@@ -240,7 +243,7 @@ __global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS4>())
         double sum = 0.0;
         int cnt = 0;
 #pragma unroll
-        for (int s = 0; s < NS; ++s)
+        for (int s = 0; s < NV; ++s)
           if (v[s] > Ht) { sum += (double)v[s] - Md; ++cnt; }
         cnt = group_sum<G>(cnt, gmask);
         sum = group_sum<G>(sum, gmask);
@@ -258,42 +261,42 @@ __global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS4>())
       // Support entries first; the label entry is rewritten by lane 0 after a
       // group barrier (which orders the two stores to that address).
       const float inv = (float)((double)a.scale / (double)kap);
-      float* gr = a.grad + row * a.ld;
+      T* gr = static_cast<T*>(a.grad) + row * a.ld;
 #pragma unroll
-      for (int i = 0; i < NS4; ++i) {
-        float g[4];
+      for (int i = 0; i < NS; ++i) {
+        float g[EPS];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) g[j] = (v[4 * i + j] > Hf) ? inv : 0.0f;
-        warp_tier_store4<G, VEC, FULL4>(gr, i, li, C, g);
+        for (int j = 0; j < EPS; ++j) g[j] = (v[EPS * i + j] > Hf) ? inv : 0.0f;
+        warp_tier_store_slot<T, G, VEC, FULLV>(gr, i, li, C, g);
       }
       if (yok) {
         __syncwarp(gmask);
-        if (li == 0) gr[yc] = ((zy > Hf) ? inv : 0.0f) - a.scale;
+        if (li == 0) st_elem(gr + yc, ((zy > Hf) ? inv : 0.0f) - a.scale);
       }
     } else if (OUT == kOutMask) {
       uint8_t* mr = a.mask + row * a.C;
 #pragma unroll
-      for (int i = 0; i < NS4; ++i) {
+      for (int i = 0; i < NS; ++i) {
         uint8_t b[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) b[j] = (v[4 * i + j] > Hf) ? 1 : 0;
-        warp_tier_store4_mask<G, VEC, FULL4>(mr, i, li, C, a.mask_vec, b);
+        warp_tier_store_mask<G, VEC, FULLV>(mr, i, li, C, a.mask_vec, b);
       }
     } else {  // kOutCand
       int cnt = 0;
 #pragma unroll
-      for (int s = 0; s < NS; ++s) cnt += (v[s] > Hf) ? 1 : 0;
+      for (int s = 0; s < NV; ++s) cnt += (v[s] > Hf) ? 1 : 0;
       int off = group_excl_scan<G>(cnt, li, gmask);
       float* cv = a.cand_val + row * a.C;
       int32_t* ci = a.cand_idx + row * a.C;
       if (cnt > 0) {
 #pragma unroll
-        for (int i = 0; i < NS4; ++i)
+        for (int i = 0; i < NS; ++i)
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            if (v[4 * i + j] > Hf) {
-              cv[off] = v[4 * i + j];
-              ci[off] = group_slot_col<G, VEC>(i, j, li);
+          for (int j = 0; j < EPS; ++j)
+            if (v[EPS * i + j] > Hf) {
+              cv[off] = v[EPS * i + j];
+              ci[off] = group_slot_col<G, EPS, VEC>(i, j, li);
               ++off;
             }
       }

@@ -29,7 +29,12 @@ _SIGS = {
     "fw_backward_candidates": ([_P, _P, _P, _P, _P, _P, _I64, _I64, ctypes.c_float, _P, _P, _P], ctypes.c_int),
     "fw_scale_grad": ([_P, _P, ctypes.c_int, ctypes.c_float, _I64, _I64, _I64, _P], ctypes.c_int),
     "fw_loss_reduce": ([_P, _I64, ctypes.c_double, _P, _P], ctypes.c_int),
+    "fw_fused_fwd_bwd_typed": ([ctypes.c_int, _P, _P, _I64, _I64, _I64, ctypes.c_float, _P, _P, _P, _P,
+                                _P, _P], ctypes.c_int),
+    "fw_scale_grad_typed": ([ctypes.c_int, _P, _P, ctypes.c_int, ctypes.c_float, _I64, _I64, _I64, _P],
+                            ctypes.c_int),
 }
+DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 EXPORTED = tuple(_SIGS)
 
 _lib = None
@@ -71,9 +76,10 @@ def _check(rc, what):
         raise FWError(f"{what}: {load().fw_error_string(rc).decode()} (code {rc})")
 
 
-def _rows(z):
-    if z.dim() != 2 or z.dtype != torch.float32 or not z.is_cuda:
-        raise FWError("logits must be a 2-D float32 CUDA tensor")
+def _rows(z, any_float=False):
+    if z.dim() != 2 or not z.is_cuda or z.dtype not in (DTYPE_CODES if any_float else (torch.float32,)):
+        raise FWError("logits must be a 2-D float32 CUDA tensor" +
+                      (" (or bfloat16 / float16)" if any_float else ""))
     if z.stride(1) != 1 or (z.size(0) > 1 and z.stride(0) < z.size(1)):
         z = z.contiguous()
     ld = z.stride(0) if z.size(0) > 1 else z.size(1)
@@ -81,19 +87,26 @@ def _rows(z):
 
 
 def fused_fwd_bwd(z, y, grad_scale, grad=None, status=None):
-    """(grad, H, loss, kappa) from the fused kernel; grad has z's row stride."""
-    z, ld = _rows(z)
+    """(grad, H, loss, kappa) from the fused kernel; grad has z's row stride
+    and dtype (float32 logits use fw_fused_fwd_bwd, 16-bit logits
+    fw_fused_fwd_bwd_typed)."""
+    z, ld = _rows(z, any_float=True)
     B, C = z.shape
     if grad is None:
-        grad = torch.empty_strided((B, C), (ld, 1), dtype=torch.float32, device=z.device)
+        grad = torch.empty_strided((B, C), (ld, 1), dtype=z.dtype, device=z.device)
     H = torch.empty(B, dtype=torch.float32, device=z.device)
     loss = torch.empty(B, dtype=torch.float32, device=z.device)
     kappa = torch.empty(B, dtype=torch.int32, device=z.device)
     lib = load()
     with torch.cuda.device(z.device):
-        _check(lib.fw_fused_fwd_bwd(_ptr(z), _ptr(y), B, C, ld, float(grad_scale), _ptr(grad),
-                                    _ptr(H), _ptr(loss), _ptr(kappa), _ptr(status), _stream(z)),
-               "fw_fused_fwd_bwd")
+        if z.dtype == torch.float32:
+            rc = lib.fw_fused_fwd_bwd(_ptr(z), _ptr(y), B, C, ld, float(grad_scale), _ptr(grad),
+                                      _ptr(H), _ptr(loss), _ptr(kappa), _ptr(status), _stream(z))
+        else:
+            rc = lib.fw_fused_fwd_bwd_typed(DTYPE_CODES[z.dtype], _ptr(z), _ptr(y), B, C, ld,
+                                            float(grad_scale), _ptr(grad), _ptr(H), _ptr(loss),
+                                            _ptr(kappa), _ptr(status), _stream(z))
+        _check(rc, "fw_fused_fwd_bwd")
     return grad, H, loss, kappa
 
 
@@ -150,9 +163,10 @@ def backward_candidates(cv, ci, cc, H, kappa, y, grad_scale, status=None):
 def scale_grad(grad, grad_output, per_row, assumed_scale):
     B, C = grad.shape
     ld = grad.stride(0) if B > 1 else C
+    go = grad_output.to(torch.float32)
     with torch.cuda.device(grad.device):
-        _check(load().fw_scale_grad(_ptr(grad), _ptr(grad_output), int(bool(per_row)),
-                                    float(assumed_scale), B, C, ld, _stream(grad)), "fw_scale_grad")
+        _check(load().fw_scale_grad_typed(DTYPE_CODES[grad.dtype], _ptr(grad), _ptr(go), int(bool(per_row)),
+                                          float(assumed_scale), B, C, ld, _stream(grad)), "fw_scale_grad")
     return grad
 
 

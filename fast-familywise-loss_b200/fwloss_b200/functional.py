@@ -23,8 +23,8 @@ _REDUCTIONS = ("mean", "sum", "none")
 def _check_inputs(logits, target):
     if not (isinstance(logits, torch.Tensor) and logits.is_cuda):
         raise TypeError("familywise_loss: logits must be a CUDA tensor (this build has no CPU path)")
-    if logits.dim() != 2 or logits.dtype != torch.float32:
-        raise TypeError("familywise_loss: logits must be a 2-D float32 tensor [N, K]")
+    if logits.dim() != 2 or logits.dtype not in (torch.float32, torch.bfloat16, torch.float16):
+        raise TypeError("familywise_loss: logits must be a 2-D float32, bfloat16 or float16 tensor [N, K]")
     if target.dim() != 1 or target.shape[0] != logits.shape[0]:
         raise ValueError("familywise_loss: target must have shape [N]")
     if target.dtype != torch.int64:
@@ -46,6 +46,8 @@ class _FWRows(torch.autograd.Function):
         ctx.grad = grad
         ctx.assumed = float(assumed)
         ctx.mark_non_differentiable(H, kappa)
+        if logits.dtype != torch.float32:  # losses in the logits' dtype, like torch losses
+            losses = losses.to(logits.dtype)
         return losses, H, kappa
 
     @staticmethod
@@ -65,7 +67,8 @@ class _FWReduced(torch.autograd.Function):
     def forward(ctx, logits, target, scale, status):
         grad, H, losses, kappa = ext().fused_fwd_bwd(logits.detach(), target, float(scale), status)
         ctx.grad = grad
-        return ext().loss_reduce(losses, float(scale))
+        out = ext().loss_reduce(losses, float(scale))
+        return out if logits.dtype == torch.float32 else out.to(logits.dtype)
 
     @staticmethod
     def backward(ctx, g):
@@ -81,7 +84,8 @@ class _MeanOfRows(torch.autograd.Function):
     @staticmethod
     def forward(ctx, losses):
         ctx.n = losses.shape[0]
-        return ext().loss_reduce(losses, 1.0 / ctx.n if ctx.n else float("nan"))
+        out = ext().loss_reduce(losses.float(), 1.0 / ctx.n if ctx.n else float("nan"))
+        return out if losses.dtype == torch.float32 else out.to(losses.dtype)
 
     @staticmethod
     def backward(ctx, g):
@@ -92,6 +96,8 @@ def familywise_loss(logits, target, reduction="mean", status=None):
     """FW loss of logits [N, K] (fp32, CUDA) against int64 targets [N].
 
     reduction "mean" / "sum" return a 0-d tensor, "none" the per-row losses.
+    bfloat16 / float16 logits are accepted (fp32 arithmetic; gradient and loss
+    in the logits' dtype).
     `status`, if given, is an int32 CUDA tensor whose first word receives the
     bit-or of FWB_STATUS_* flags (label out of range, non-finite row).
     """

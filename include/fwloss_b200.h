@@ -45,6 +45,14 @@ extern "C" {
 #define FWB_E_POINTER 2    /* a required pointer is NULL                       */
 #define FWB_E_LAUNCH 3     /* the CUDA launch failed (cudaGetLastError)        */
 #define FWB_E_CAPACITY 4   /* a size exceeds a stated maximum                  */
+#define FWB_E_DTYPE 5      /* unknown element type code                        */
+
+/* Element types of logits / gradient for the *_typed entry points (the
+ * arithmetic is fp32/fp64 for all of them; 16-bit values are passed as their
+ * bit patterns). */
+#define FWB_DTYPE_F32 0
+#define FWB_DTYPE_BF16 1
+#define FWB_DTYPE_F16 2
 
 #define FWB_STATUS_LABEL_RANGE 1   /* some label y[r] is outside [0, C)          */
 #define FWB_STATUS_NONFINITE 2     /* some row maximum is NaN or +-inf           */
@@ -71,6 +79,20 @@ FWB_API int fw_fused_fwd_bwd(const float* z, const int64_t* y, int64_t B, int64_
                      int64_t ld, float grad_scale, float* grad, float* H,
                      float* loss, int32_t* kappa, int32_t* status,
                      void* stream);
+
+/*
+ * fw_fused_fwd_bwd for logits of element type `dtype` (FWB_DTYPE_*); the
+ * gradient has the same element type and the logits' row stride, H and loss
+ * stay fp32.  16-bit logits halve the bytes per row; the threshold, kappa
+ * and the loss are computed exactly from the 16-bit values.  Extends the
+ * reference's fp32-only entry points (src/cuda/fw_radix_argmax.cu:1387,1422
+ * reject other dtypes); the CPU kernel's dtype dispatch
+ * (src/cpu/fw_cpu.cpp:698-704) covers fp32/fp64.
+ */
+FWB_API int fw_fused_fwd_bwd_typed(int dtype, const void* z, const int64_t* y, int64_t B,
+                                   int64_t C, int64_t ld, float grad_scale, void* grad,
+                                   float* H, float* loss, int32_t* kappa, int32_t* status,
+                                   void* stream);
 
 /*
  * Forward producing the boolean support mask (uint8, [B, C] contiguous):
@@ -130,6 +152,11 @@ FWB_API int fw_backward_candidates(const float* cand_val, const int32_t* cand_id
 FWB_API int fw_scale_grad(float* grad, const float* grad_output, int per_row,
                   float assumed_scale, int64_t B, int64_t C, int64_t ld,
                   void* stream);
+
+/* fw_scale_grad for a gradient of element type `dtype` (FWB_DTYPE_*). */
+FWB_API int fw_scale_grad_typed(int dtype, void* grad, const float* grad_output, int per_row,
+                                float assumed_scale, int64_t B, int64_t C, int64_t ld,
+                                void* stream);
 
 /*
  * Deterministic (fixed-order, fp64) reduction out[0] = scale * sum_r loss[r].

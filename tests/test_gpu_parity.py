@@ -233,3 +233,53 @@ def test_full_size_configs(name):
     _full_size_properties(z, y, grad, H, loss, kappa, 1.0 / B)
     del grad
     torch.cuda.empty_cache()
+
+
+HALF_TYPES = {"bf16": (torch.bfloat16, 2.0 ** -8), "f16": (torch.float16, 2.0 ** -11)}
+
+
+@pytest.mark.parametrize("dtype", list(HALF_TYPES))
+@pytest.mark.parametrize("name", ["gauss_C37", "gauss_C128", "gauss_C1000", "gauss_C2048", "gauss_mid_C3000",
+                                  "gauss_mid_C31623", "gauss_mid_C32000", "ties_C128", "ties_C5000",
+                                  "dense_s1e-1_C3000", "dense_s1e-3_C1000", "dense_s1e-3_C40000",
+                                  "exact_ties", "neginf_C12000"])
+def test_half_precision_logits(dtype, name):
+    """16-bit logits: the oracle runs on the rounded values, so kappa, the
+    support, H and the loss must match as for fp32; the gradient carries the
+    element type's rounding (relative tolerance = its unit roundoff)."""
+    tdt, rtol = HALF_TYPES[dtype]
+    z32, y = dict(PARITY)[name]()
+    zh = torch.from_numpy(z32).to(tdt)
+    z = zh.float().numpy()  # the values the kernel sees
+    B = len(y)
+    ref = O.solve(z, y, 1.0 / B)
+    zt = zh.cuda()
+    yt = torch.from_numpy(y).cuda()
+    grad, H, loss, kappa = capi.fused_fwd_bwd(zt, yt, 1.0 / B)
+    torch.cuda.synchronize()
+    assert grad.dtype == tdt
+    np.testing.assert_array_equal(kappa.cpu().numpy(), ref["kappa"], err_msg=name)
+    np.testing.assert_allclose(H.cpu().numpy(), ref["H"], rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(loss.cpu().numpy(), ref["loss"], rtol=RTOL, atol=ATOL)
+    np.testing.assert_array_equal((z > H.cpu().numpy()[:, None]), ref["mask"])
+    np.testing.assert_allclose(grad.float().cpu().numpy(), ref["grad"], rtol=rtol, atol=ATOL)
+    # device-side upstream scaling on the 16-bit gradient
+    capi.scale_grad(grad, torch.tensor([2.0], device="cuda"), False, 1.0)
+    np.testing.assert_allclose(grad.float().cpu().numpy(), 2.0 * ref["grad"], rtol=2 * rtol, atol=ATOL)
+
+
+@pytest.mark.parametrize("dtype", list(HALF_TYPES))
+def test_half_precision_autograd(dtype):
+    from fwloss_b200 import familywise_loss
+
+    tdt, rtol = HALF_TYPES[dtype]
+    z32, y = cases.gauss(64, 5000, 1.0, seed=77)()
+    zh = torch.from_numpy(z32).to(tdt)
+    ref = O.solve(zh.float().numpy(), y, 1.0 / 64)
+    z = zh.cuda().requires_grad_(True)
+    out = familywise_loss(z, torch.from_numpy(y).cuda(), reduction="mean")
+    assert out.dtype == tdt
+    out.backward()
+    assert z.grad.dtype == tdt
+    np.testing.assert_allclose(out.float().item(), ref["loss"].mean(), rtol=rtol)
+    np.testing.assert_allclose(z.grad.float().cpu().numpy(), ref["grad"], rtol=rtol, atol=ATOL)
