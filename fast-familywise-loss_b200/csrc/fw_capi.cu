@@ -18,6 +18,7 @@
 #include "../../include/fwloss_b200.h"
 #include "fw_aux.cuh"
 #include "fw_device.cuh"
+#include "fw_shard.cuh"
 #include "fw_stream_tier.cuh"
 #include "fw_warp_tier.cuh"
 
@@ -297,6 +298,61 @@ int fw_scale_grad_typed(int dtype, void* grad, const float* grad_output, int per
     e = launch(fw_scale_grad_kernel<float>, grid, block, 1, st, static_cast<float*>(grad),
                grad_output, per_row, assumed_scale, B, C, ld, vec);
   return launch_status(e);
+}
+
+int fw_shard_scan(const float* z, int64_t B, int64_t C_local, int64_t ld, int K, float* grad,
+                  int32_t* summary, int32_t* local_idx, void* stream) {
+  if (int rc = check_shape(B, C_local, ld)) return rc;
+  if (K < 1 || K > kShardMaxK) return FWB_E_CAPACITY;
+  if (B > 0 && (!z || !grad || !summary || !local_idx)) return FWB_E_POINTER;
+  RowArgs a = base_args(z, nullptr, B, C_local, ld, nullptr, nullptr, nullptr, nullptr);
+  a.grad = grad;
+  a.shard_sum = summary;
+  a.shard_idx = local_idx;
+  a.shard_k = K;
+  const bool vec = aligned16(z) && aligned16(grad) && (ld % 4 == 0);
+  return run_rows<float, kOutShard>(a, static_cast<cudaStream_t>(stream), vec);
+}
+
+int fw_shard_solve(const int32_t* gathered, int nranks, int rank, const int64_t* col_start,
+                   int64_t B, int K, const float* z, int64_t ld, const int64_t* y,
+                   float grad_scale, float* grad, const int32_t* local_idx, float* H,
+                   int32_t* kappa, float* loss_part, int32_t* fb_rows, int32_t* fb_count,
+                   int32_t* status, void* stream) {
+  if (nranks < 1 || nranks > kMaxShards || rank < 0 || rank >= nranks || !col_start) return FWB_E_SHAPE;
+  if (K < 1 || K > kShardMaxK || nranks * K > kShardListCap) return FWB_E_CAPACITY;
+  if (col_start[0] != 0) return FWB_E_SHAPE;
+  for (int q = 0; q < nranks; ++q)
+    if (col_start[q + 1] <= col_start[q]) return FWB_E_SHAPE;
+  const int64_t C_local = col_start[rank + 1] - col_start[rank];
+  if (int rc = check_shape(B, C_local, ld)) return rc;
+  if (!fb_count) return FWB_E_POINTER;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(fb_count, 0, sizeof(int32_t), st) != cudaSuccess) return FWB_E_LAUNCH;
+  if (B == 0) return FWB_OK;
+  if (!gathered || !z || !y || !grad || !local_idx || !fb_rows) return FWB_E_POINTER;
+  ShardSolveArgs a = {};
+  a.gathered = gathered;
+  a.nranks = nranks;
+  a.rank = rank;
+  a.K = K;
+  a.B = B;
+  for (int q = 0; q <= nranks; ++q) a.col_start[q] = col_start[q];
+  a.z = z;
+  a.ld = ld;
+  a.y = y;
+  a.scale = grad_scale;
+  a.grad = grad;
+  a.local_idx = local_idx;
+  a.H = H;
+  a.kappa = kappa;
+  a.loss_part = loss_part;
+  a.fb_rows = fb_rows;
+  a.fb_count = fb_count;
+  a.status = status;
+  const int warps = kShardSolveThreads / 32;
+  return launch_status(launch(fw_shard_solve_kernel, dim3(aux_grid(B, warps)), dim3(kShardSolveThreads), 1,
+                              st, a));
 }
 
 int fw_loss_reduce(const float* loss, int64_t B, double scale, float* out, void* stream) {

@@ -26,7 +26,18 @@ constexpr unsigned kFull = 0xffffffffu;
 
 // Output of the forward search: the gradient row, the support mask, or the
 // support as a (value, column) list.
-enum OutMode : int { kOutGrad = 0, kOutMask = 1, kOutCand = 2 };
+// kOutShard: one column shard of a class-sharded row (fw_shard.cuh): zero
+// gradient shard, plus a summary record of the shard's own solve.
+enum OutMode : int { kOutGrad = 0, kOutMask = 1, kOutCand = 2, kOutShard = 3 };
+
+// Summary record of one row of one class shard (int32 words):
+//   [0] local maximum M_r (float bits)   [1] local support size kappa_r
+//   [2] flags (bit 0: M_r is NaN or +-inf)
+//   [3] local column of the first maximal element when bit 0 is set
+//   [4 .. 4+K) the values (float bits) of the first min(kappa_r, K) local
+//   support elements; their local columns go to a separate [B, K] array.
+constexpr int kShardHeader = 4;
+constexpr int kShardNonFinite = 1;
 
 // Element types of logits and gradient.  Arithmetic is fp32/fp64 for all of
 // them; a 16-byte slot holds kEPS elements.
@@ -119,6 +130,9 @@ struct RowArgs {
   int32_t* kappa;        // [B] or null
   int32_t* status;       // device word or null
   int mask_vec;          // mask rows are 4-byte aligned (C % 4 == 0)
+  int32_t* shard_sum;    // kOutShard: [B, kShardHeader + shard_k]
+  int32_t* shard_idx;    // kOutShard: [B, shard_k]
+  int shard_k;           // kOutShard: support entries kept per row
 };
 
 // max() that returns NaN when either input is NaN (fmaxf would drop it).

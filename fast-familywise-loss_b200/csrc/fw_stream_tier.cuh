@@ -212,7 +212,8 @@ __device__ __forceinline__ void for_each_element(const T* zr, int64_t C,
 template <class T, int CS, bool VEC, int OUT>
 __global__ void __launch_bounds__(kST)
     fw_stream_rows_kernel(RowArgs a) {
-  static_assert(OUT == kOutGrad || sizeof(T) == 4, "mask/candidate outputs are fp32-only");
+  static_assert(OUT == kOutGrad || sizeof(T) == 4, "mask/candidate/shard outputs are fp32-only");
+  constexpr bool kZeroFill = (OUT == kOutGrad || OUT == kOutShard);
   constexpr int EPS = Elem<T>::kEPS;
   __shared__ StreamShared s;
   const int tid = threadIdx.x;
@@ -243,7 +244,7 @@ __global__ void __launch_bounds__(kST)
   bool ovf = false;
   float* lz = s.lz[w];
   int* li = s.li[w];
-  T* gr = (OUT == kOutGrad) ? static_cast<T*>(a.grad) + row * a.ld : nullptr;
+  T* gr = kZeroFill ? static_cast<T*>(a.grad) + row * a.ld : nullptr;
   uint8_t* mr = (OUT == kOutMask) ? a.mask + row * C : nullptr;
 
   for (int64_t base = g.i0; base < g.i1; base += (int64_t)kST * IPT) {
@@ -266,7 +267,7 @@ __global__ void __launch_bounds__(kST)
     for (int u = 0; u < IPT; ++u) {
       const int64_t it = base + (int64_t)u * kST + tid;
       if (it < g.i1) {
-        if (OUT == kOutGrad) {
+        if (kZeroFill) {
           if (VEC)
             *reinterpret_cast<uint4*>(gr + W * it) = make_uint4(0u, 0u, 0u, 0u);
           else
@@ -308,7 +309,7 @@ __global__ void __launch_bounds__(kST)
     const bool in = c < C;
     const float x = in ? ld_elem(zr + c) : -CUDART_INF_F;
     if (in) {
-      if (OUT == kOutGrad) st_elem(gr + c, 0.0f);
+      if (kZeroFill) st_elem(gr + c, 0.0f);
       if (OUT == kOutMask) mr[c] = 0;
     }
     run = max_nan(run, warp_max_nan(x));
@@ -346,7 +347,7 @@ __global__ void __launch_bounds__(kST)
   const float M = s.row_max;
   const double Md = (double)M;
   const float t0 = __fsub_rd(M, 1.0f);
-  const int64_t ylab = a.y[row];
+  const int64_t ylab = a.y ? a.y[row] : -1;  // no labels in kOutShard
   const bool yok = (ylab >= 0 && ylab < C);
   const int yc = yok ? (int)ylab : -1;
 
@@ -374,10 +375,21 @@ __global__ void __launch_bounds__(kST)
       if (yok && j != yc) st_elem(gr + yc, -a.scale);
     } else if (OUT == kOutMask) {
       mr[j] = 1;
-    } else {
+    } else if (OUT == kOutCand) {
       a.cand_val[row * C] = ld_elem(zr + j);
       a.cand_idx[row * C] = j;
       if (a.cand_count) a.cand_count[row] = 1;
+    } else {  // kOutShard: the gradient shard stays zero
+      int32_t* rec = a.shard_sum + row * (int64_t)(kShardHeader + a.shard_k);
+      rec[0] = __float_as_int(M);
+      rec[1] = 1;
+      rec[2] = kShardNonFinite;
+      rec[3] = j;
+      if (a.shard_k > 0) {
+        rec[kShardHeader] = __float_as_int(M);
+        a.shard_idx[row * (int64_t)a.shard_k] = j;
+      }
+      return;
     }
     if (a.H) a.H[row] = M;
     if (a.loss) a.loss[row] = yok ? (1.0f - zy + M) : CUDART_NAN_F;
@@ -453,6 +465,29 @@ __global__ void __launch_bounds__(kST)
     } else if (OUT == kOutMask) {
       for (int k = lane; k < n; k += 32)
         if (s.sz[k] > Hf) mr[s.si[k]] = 1;
+    } else if (OUT == kOutShard) {
+      const int K = a.shard_k;
+      int32_t* rec = a.shard_sum + row * (int64_t)(kShardHeader + K);
+      int32_t* ridx = a.shard_idx + row * (int64_t)K;
+      int pos0 = 0;
+      for (int k0 = 0; k0 < n && pos0 < K; k0 += 32) {
+        const int k = k0 + lane;
+        const bool sel = (k < n) && (s.sz[k] > Hf);
+        const unsigned b = __ballot_sync(kFull, sel);
+        const int pos = pos0 + __popc(b & lanemask_lt(lane));
+        if (sel && pos < K) {
+          rec[kShardHeader + pos] = __float_as_int(s.sz[k]);
+          ridx[pos] = s.si[k];
+        }
+        pos0 += __popc(b);
+      }
+      if (lane == 0) {
+        rec[0] = __float_as_int(M);
+        rec[1] = kap;
+        rec[2] = 0;
+        rec[3] = -1;
+      }
+      return;
     } else {
       float* cv = a.cand_val + row * C;
       int32_t* ci = a.cand_idx + row * C;
@@ -583,6 +618,28 @@ __global__ void __launch_bounds__(kST)
     });
   } else if (OUT == kOutMask) {
     for_each_element<T, CS, VEC>(zr, C, rank, [&](float x, int c) { mr[c] = sel_of(x) ? 1 : 0; });
+  } else if (OUT == kOutShard) {
+    int* pos_ctr = &cta_smem<CS>(&s, 0)->cand_pos;
+    const int K = a.shard_k;
+    int32_t* rec = a.shard_sum + row * (int64_t)(kShardHeader + K);
+    int32_t* ridx = a.shard_idx + row * (int64_t)K;
+    for_each_element<T, CS, VEC>(zr, C, rank, [&](float x, int c) {
+      if (sel_of(x)) {
+        const int p = atomicAdd(pos_ctr, 1);
+        if (p < K) {
+          rec[kShardHeader + p] = __float_as_int(x);
+          ridx[p] = c;
+        }
+      }
+    });
+    row_barrier<CS>();
+    if (leader && tid == 0) {
+      rec[0] = __float_as_int(M);
+      rec[1] = kap;
+      rec[2] = 0;
+      rec[3] = -1;
+    }
+    return;
   } else {
     int* pos_ctr = &cta_smem<CS>(&s, 0)->cand_pos;
     float* cv = a.cand_val + row * C;

@@ -14,7 +14,7 @@
 //   * candidate_buffer/indices rows hold exactly the support (kappa entries),
 //     so fw_backward needs no zero-initialised [N,K] buffer.
 // Extra functions used by the autograd layer (fwloss_b200 package):
-//   fused_fwd_bwd, scale_grad, loss_reduce.
+//   fused_fwd_bwd, scale_grad, loss_reduce, shard_scan, shard_solve.
 #include <torch/extension.h>
 
 #include <ATen/cuda/CUDAContext.h>
@@ -243,6 +243,64 @@ torch::Tensor loss_reduce(torch::Tensor losses, double scale) {
   return out;
 }
 
+// Class-sharded step 1: (grad shard zero-filled, summary [B, 4+K], local_idx [B, K]).
+std::vector<torch::Tensor> shard_scan(torch::Tensor z_local, int64_t K) {
+  check_logits(z_local);
+  const c10::cuda::CUDAGuard guard(z_local.device());
+  const int64_t N = z_local.size(0), C = z_local.size(1);
+  int64_t ld = C;
+  auto z = rows_view(z_local, &ld);
+  auto grad = (ld == C) ? torch::empty({N, C}, z.options()) : torch::empty_strided({N, C}, {ld, 1}, z.options());
+  auto summary = torch::empty({N, 4 + K}, i32(z));
+  auto local_idx = torch::empty({N, K}, i32(z));
+  check_rc(fw_shard_scan(z.data_ptr<float>(), N, C, ld, (int)K, grad.data_ptr<float>(),
+                         summary.data_ptr<int32_t>(), local_idx.data_ptr<int32_t>(), cur_stream()),
+           "fw_shard_scan");
+  return {grad, summary, local_idx};
+}
+
+// Class-sharded step 3: (H, kappa, loss_part, fb_rows, fb_count); patches grad in place.
+std::vector<torch::Tensor> shard_solve(torch::Tensor gathered, int64_t rank, std::vector<int64_t> col_start,
+                                       torch::Tensor z_local, torch::Tensor targets, double grad_scale,
+                                       torch::Tensor grad, torch::Tensor local_idx,
+                                       c10::optional<torch::Tensor> status) {
+  check_logits(z_local);
+  const c10::cuda::CUDAGuard guard(z_local.device());
+  const int64_t N = z_local.size(0);
+  check_targets(targets, N, z_local);
+  const int64_t nranks = (int64_t)col_start.size() - 1;
+  TORCH_CHECK(gathered.is_cuda() && gathered.scalar_type() == torch::kInt32 && gathered.dim() == 3 &&
+                  gathered.size(0) == nranks && gathered.size(1) == N,
+              "gathered must be int32 [nranks, B, 4 + K]");
+  const int64_t K = gathered.size(2) - 4;
+  TORCH_CHECK(local_idx.is_cuda() && local_idx.scalar_type() == torch::kInt32 && local_idx.numel() == N * K,
+              "local_idx must be int32 [B, K]");
+  TORCH_CHECK(grad.is_cuda() && grad.scalar_type() == torch::kFloat32 && grad.stride(1) == 1 &&
+                  grad.size(0) == N && grad.size(1) == z_local.size(1),
+              "grad must be the float32 gradient shard");
+  int64_t ld = z_local.size(1);
+  auto z = rows_view(z_local, &ld);
+  const int64_t gld = N > 1 ? grad.stride(0) : grad.size(1);
+  TORCH_CHECK(gld == ld, "grad and logits shards must share the row stride");
+  auto g = gathered.contiguous();
+  auto li = local_idx.contiguous();
+  auto y = targets.contiguous();
+  auto H = torch::empty({N}, z.options());
+  auto kappa = torch::empty({N}, i32(z));
+  auto loss_part = torch::empty({N}, z.options());
+  auto fb_rows = torch::empty({N > 0 ? N : 1}, i32(z));
+  auto fb_count = torch::empty({1}, i32(z));
+  int32_t* st = nullptr;
+  if (status.has_value()) st = status->data_ptr<int32_t>();
+  check_rc(fw_shard_solve(g.data_ptr<int32_t>(), (int)nranks, (int)rank, col_start.data(), N, (int)K,
+                          z.data_ptr<float>(), ld, y.data_ptr<int64_t>(), (float)grad_scale,
+                          grad.data_ptr<float>(), li.data_ptr<int32_t>(), H.data_ptr<float>(),
+                          kappa.data_ptr<int32_t>(), loss_part.data_ptr<float>(), fb_rows.data_ptr<int32_t>(),
+                          fb_count.data_ptr<int32_t>(), st, cur_stream()),
+           "fw_shard_solve");
+  return {H, kappa, loss_part, fb_rows, fb_count};
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "B200 (sm_100a) Familywise loss: drop-in for the fw_radix_cuda module";
   m.def("fw_forward", &fw_forward, "FW forward (support as candidate lists)");
@@ -253,5 +311,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("logits"), py::arg("targets"), py::arg("grad_scale"), py::arg("status") = py::none());
   m.def("scale_grad", &scale_grad, "in-place grad scaling by a device-side grad_output");
   m.def("loss_reduce", &loss_reduce, "deterministic scale * sum(losses)");
+  m.def("shard_scan", &shard_scan, "class-sharded step 1: local solve, zero gradient shard, summaries");
+  m.def("shard_solve", &shard_solve, "class-sharded step 3: global solve from gathered summaries",
+        py::arg("gathered"), py::arg("rank"), py::arg("col_start"), py::arg("z_local"), py::arg("targets"),
+        py::arg("grad_scale"), py::arg("grad"), py::arg("local_idx"), py::arg("status") = py::none());
   m.def("version", []() { return std::string(fw_version()); });
 }

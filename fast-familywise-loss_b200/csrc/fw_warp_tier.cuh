@@ -126,10 +126,29 @@ __device__ __forceinline__ void warp_tier_nonfinite(const RowArgs& a, int64_t ro
       for (int j = 0; j < 4; ++j) b[j] = (group_slot_col<G, 4, VEC>(i, j, li) == jstar) ? 1 : 0;
       warp_tier_store_mask<G, VEC, false>(mr, i, li, C, a.mask_vec, b);
     }
-  } else if (li == 0) {
-    a.cand_val[row * a.C] = ld_elem(static_cast<const T*>(a.z) + row * a.ld + jstar);
-    a.cand_idx[row * a.C] = jstar;
-    if (a.cand_count) a.cand_count[row] = 1;
+  } else if (OUT == kOutCand) {
+    if (li == 0) {
+      a.cand_val[row * a.C] = ld_elem(static_cast<const T*>(a.z) + row * a.ld + jstar);
+      a.cand_idx[row * a.C] = jstar;
+      if (a.cand_count) a.cand_count[row] = 1;
+    }
+  } else {  // kOutShard: zero gradient shard, summary of a non-finite row
+    T* gr = static_cast<T*>(a.grad) + row * a.ld;
+    const float zero[Elem<T>::kEPS] = {};
+#pragma unroll
+    for (int i = 0; i < NS; ++i) warp_tier_store_slot<T, G, VEC, false>(gr, i, li, C, zero);
+    if (li == 0) {
+      int32_t* rec = a.shard_sum + row * (int64_t)(kShardHeader + a.shard_k);
+      rec[0] = __float_as_int(m);
+      rec[1] = 1;
+      rec[2] = kShardNonFinite;
+      rec[3] = jstar;
+      if (a.shard_k > 0) {
+        rec[kShardHeader] = __float_as_int(m);
+        a.shard_idx[row * (int64_t)a.shard_k] = jstar;
+      }
+    }
+    return;
   }
   if (li == 0) {
     if (a.H) a.H[row] = m;
@@ -154,7 +173,7 @@ __global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS * El
   constexpr int NV = NS * EPS;          // register values per lane
   constexpr int RPW = 32 / G;           // rows per warp
   constexpr int CAPG = kWarpListCap / RPW;
-  static_assert(OUT == kOutGrad || sizeof(T) == 4, "mask/candidate outputs are fp32-only");
+  static_assert(OUT == kOutGrad || sizeof(T) == 4, "mask/candidate/shard outputs are fp32-only");
   __shared__ float s_list[kWarpTierWarps][kWarpListCap];
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
@@ -169,7 +188,7 @@ __global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS * El
   for (int64_t row = ((int64_t)blockIdx.x * kWarpTierWarps + wib) * RPW + gi; row < a.B;
        row += ngroups) {
     const T* zr = zbase + row * a.ld;
-    const int64_t ylab = a.y[row];
+    const int64_t ylab = a.y ? a.y[row] : -1;  // no labels in kOutShard
     float v[NV];
 #pragma unroll
     for (int i = 0; i < NS; ++i) {
@@ -282,6 +301,39 @@ __global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS * El
         for (int j = 0; j < 4; ++j) b[j] = (v[4 * i + j] > Hf) ? 1 : 0;
         warp_tier_store_mask<G, VEC, FULLV>(mr, i, li, C, a.mask_vec, b);
       }
+    } else if (OUT == kOutShard) {
+      // zero gradient shard; the support goes to the summary record
+      T* gr = static_cast<T*>(a.grad) + row * a.ld;
+      const float zero[EPS] = {};
+#pragma unroll
+      for (int i = 0; i < NS; ++i) warp_tier_store_slot<T, G, VEC, FULLV>(gr, i, li, C, zero);
+      int cnt = 0;
+#pragma unroll
+      for (int s = 0; s < NV; ++s) cnt += (v[s] > Hf) ? 1 : 0;
+      int off = group_excl_scan<G>(cnt, li, gmask);
+      const int K = a.shard_k;
+      int32_t* rec = a.shard_sum + row * (int64_t)(kShardHeader + K);
+      int32_t* ridx = a.shard_idx + row * (int64_t)K;
+      if (cnt > 0 && off < K) {
+#pragma unroll
+        for (int i = 0; i < NS; ++i)
+#pragma unroll
+          for (int j = 0; j < EPS; ++j)
+            if (v[EPS * i + j] > Hf) {
+              if (off < K) {
+                rec[kShardHeader + off] = __float_as_int(v[EPS * i + j]);
+                ridx[off] = group_slot_col<G, EPS, VEC>(i, j, li);
+              }
+              ++off;
+            }
+      }
+      if (li == 0) {
+        rec[0] = __float_as_int(m);
+        rec[1] = kap;
+        rec[2] = 0;
+        rec[3] = -1;
+      }
+      continue;
     } else {  // kOutCand
       int cnt = 0;
 #pragma unroll

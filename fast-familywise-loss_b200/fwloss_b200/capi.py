@@ -34,7 +34,11 @@ _SIGS = {
     "fw_scale_grad_typed": ([ctypes.c_int, _P, _P, ctypes.c_int, ctypes.c_float, _I64, _I64, _I64, _P],
                             ctypes.c_int),
 }
+_SIGS["fw_shard_scan"] = ([_P, _I64, _I64, _I64, ctypes.c_int, _P, _P, _P, _P], ctypes.c_int)
+_SIGS["fw_shard_solve"] = ([_P, ctypes.c_int, ctypes.c_int, _P, _I64, ctypes.c_int, _P, _I64, _P,
+                           ctypes.c_float, _P, _P, _P, _P, _P, _P, _P, _P, _P], ctypes.c_int)
 DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+
 EXPORTED = tuple(_SIGS)
 
 _lib = None
@@ -176,3 +180,37 @@ def loss_reduce(loss, scale):
         _check(load().fw_loss_reduce(_ptr(loss), loss.numel(), float(scale), _ptr(out),
                                      _stream(loss)), "fw_loss_reduce")
     return out
+
+
+def shard_scan(z, K):
+    """Class-sharded step 1 on this rank's shard: (grad shard, summary, local_idx)."""
+    z, ld = _rows(z)
+    B, C = z.shape
+    grad = torch.empty_strided((B, C), (ld, 1), dtype=torch.float32, device=z.device)
+    summary = torch.empty((B, 4 + K), dtype=torch.int32, device=z.device)
+    local_idx = torch.empty((B, K), dtype=torch.int32, device=z.device)
+    with torch.cuda.device(z.device):
+        _check(load().fw_shard_scan(_ptr(z), B, C, ld, int(K), _ptr(grad), _ptr(summary), _ptr(local_idx),
+                                    _stream(z)), "fw_shard_scan")
+    return grad, summary, local_idx
+
+
+def shard_solve(gathered, rank, col_start, z, y, grad_scale, grad, local_idx, status=None):
+    """Class-sharded step 3: (H, kappa, loss_part, fb_rows, fb_count); grad patched in place."""
+    z, ld = _rows(z)
+    B = z.shape[0]
+    nranks = len(col_start) - 1
+    K = gathered.shape[2] - 4
+    cs = (ctypes.c_int64 * len(col_start))(*[int(c) for c in col_start])
+    dev = z.device
+    H = torch.empty(B, dtype=torch.float32, device=dev)
+    kappa = torch.empty(B, dtype=torch.int32, device=dev)
+    loss_part = torch.empty(B, dtype=torch.float32, device=dev)
+    fb_rows = torch.empty(max(B, 1), dtype=torch.int32, device=dev)
+    fb_count = torch.empty(1, dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        _check(load().fw_shard_solve(_ptr(gathered.contiguous()), nranks, int(rank), cs, B, int(K), _ptr(z), ld,
+                                     _ptr(y), float(grad_scale), _ptr(grad), _ptr(local_idx), _ptr(H),
+                                     _ptr(kappa), _ptr(loss_part), _ptr(fb_rows), _ptr(fb_count),
+                                     _ptr(status), _stream(z)), "fw_shard_solve")
+    return H, kappa, loss_part, fb_rows, fb_count

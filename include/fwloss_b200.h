@@ -159,6 +159,44 @@ FWB_API int fw_scale_grad_typed(int dtype, void* grad, const float* grad_output,
                                 void* stream);
 
 /*
+ * Class-sharded rows (tensor-parallel LM heads): rank q of nranks holds
+ * columns [col_start[q], col_start[q+1]) of every row.  No counterpart in the
+ * reference (its rows are always whole); the math is
+ * the reference's (reference_impl.py:11-26).
+ *
+ * Step 1, on every rank: fw_shard_scan solves each row of the local shard
+ * [B, C_local] on its own, zero-fills the local gradient shard `grad`
+ * (row stride ld) and writes a summary record per row into
+ * summary[B, 4 + K] (int32 words: local max as float bits, local support size
+ * kappa_q, flags, first maximal column; then up to K support values as float
+ * bits) and the support's local columns into local_idx[B, K].  1 <= K <= 64.
+ *
+ * Step 2 (caller): all-gather the summaries of all ranks into
+ * gathered[nranks, B, 4 + K], rank-major.
+ *
+ * Step 3, on every rank: fw_shard_solve combines the summaries: the global
+ * threshold is >= every shard's own threshold, so the union of the shard
+ * supports contains the global support.  It writes H and kappa (identical on
+ * all ranks), patches this rank's gradient shard (support entries, and the
+ * label entry when y[r] falls in this rank's columns), and writes
+ * loss_part[r] = the row's loss if this rank owns the label, else 0 (sum over
+ * ranks = the per-row losses).  Rows where some shard's support exceeds K
+ * entries are not solved: their indices go to fb_rows[0 .. *fb_count)
+ * (device; *fb_count is reset by this call) for the caller to solve from the
+ * full rows.  col_start is a HOST array of nranks + 1 increasing offsets
+ * starting at 0; nranks <= 16 and nranks * K <= 256.
+ */
+FWB_API int fw_shard_scan(const float* z, int64_t B, int64_t C_local, int64_t ld, int K,
+                          float* grad, int32_t* summary, int32_t* local_idx, void* stream);
+
+FWB_API int fw_shard_solve(const int32_t* gathered, int nranks, int rank,
+                           const int64_t* col_start, int64_t B, int K, const float* z,
+                           int64_t ld, const int64_t* y, float grad_scale, float* grad,
+                           const int32_t* local_idx, float* H, int32_t* kappa,
+                           float* loss_part, int32_t* fb_rows, int32_t* fb_count,
+                           int32_t* status, void* stream);
+
+/*
  * Deterministic (fixed-order, fp64) reduction out[0] = scale * sum_r loss[r].
  * Gives the "mean" (scale 1/B) and "sum" (scale 1) values of the reference
  * (reference_impl.py:28-31, src/cuda/fw_radix_argmax.cu:1411,1493,
