@@ -61,6 +61,10 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-graph", action="store_true", help="launch steps eagerly")
+    p.add_argument("--mode", default="rows", choices=["rows", "class-sharded"],
+                   help="rows: rows sharded across GPUs (default); class-sharded: every GPU holds a "
+                        "column shard of every row (vocabulary-parallel), cfg4 shape")
+    p.add_argument("--shard-k", type=int, default=32, help="class-sharded: support entries per shard summary")
     p.add_argument("--dtype", default="f32", choices=["f32", "bf16", "f16"],
                    help="logits/gradient element type (the metric is defined on f32)")
     return p.parse_args()
@@ -449,10 +453,105 @@ def run_ours(a):
     return 0
 
 
+def run_class_sharded(a):
+    """cfg4-shaped rows (B=8192, C=128256) whose classes are split evenly across
+    the ranks; strong scaling (the whole job is one batch).  The logits are
+    drawn on the GPU from one seeded generator (identical on every rank, each
+    rank keeps its columns) with the cfg4 recipe."""
+    import torch
+    import torch.distributed as dist
+
+    from fwloss_b200._native import ext
+    from fwloss_b200.sharded import even_col_start, scan_phase, sharded_loss_step
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    B, C = 8192, 128256
+    g = torch.Generator(device=dev).manual_seed(4)
+    z = torch.randn(B, C, generator=g, device=dev)
+    y = torch.randint(0, C, (B,), generator=g, device=dev)
+    b = (y + torch.randint(1, C, (B,), generator=g, device=dev)) % C
+    z[torch.arange(B, device=dev), b] += 8.0
+    cs = even_col_start(C, world)
+    zl = z[:, cs[rank]:cs[rank + 1]].contiguous()
+    del z
+    torch.cuda.empty_cache()
+    scale = 1.0 / B
+    fw = ext()
+
+    def all_gather(x):
+        if world == 1:
+            return x.unsqueeze(0)
+        out = torch.empty((world,) + tuple(x.shape), dtype=x.dtype, device=dev)
+        dist.all_gather_into_tensor(out, x.contiguous())
+        return out
+
+    def all_reduce(t):
+        if world > 1:
+            dist.all_reduce(t)
+        return t
+
+    def step():
+        return sharded_loss_step(zl, y, cs, rank, scale, all_gather, all_reduce, a.shard_k)[1]
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(a.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    # the local scan kernel alone
+    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    k0.record(stream)
+    for _ in range(a.steps):
+        scan_phase(zl, a.shard_k)
+    k1.record(stream)
+    torch.cuda.synchronize(dev)
+    k_ms = k0.elapsed_time(k1) / a.steps
+    Cl = cs[rank + 1] - cs[rank]
+    alg = B * (8 * Cl + 4 * (4 + a.shard_k) + 4 * a.shard_k)
+    peak, peak_kind = measured_peak()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "FWLoss fwd+bwd rows/s, class-sharded rows (vocabulary-parallel)", "value": B * a.steps / (ms / 1e3),
+            "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms / a.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (cfg4 recipe, drawn on the GPU)",
+            "config": {"workload": f"B={B} x C={C}, classes split over {world} GPUs ({Cl} per GPU), K={a.shard_k}",
+                       "l2": "logits shard > L2 per GPU" if B * Cl * 4 > 3 * L2_BYTES else "logits shard < 3x L2"},
+            "roofline": {"bound": "hbm", "kernel": "shard scan (fused kernel, kOutShard)", "kernel_ms": k_ms,
+                         "achieved": alg / (k_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": alg / (k_ms / 1e3) / 1e9 / peak, "peak_kind": peak_kind},
+            "gpu_launches": 4 * a.steps,
+        }), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     a = parse()
     if a.impl == "reference":
         return run_reference(a)
+    if a.mode == "class-sharded":
+        return run_class_sharded(a)
     return run_ours(a)
 
 

@@ -107,7 +107,13 @@ __global__ void __launch_bounds__(kShardSolveThreads)
 
     const bool truncated = __any_sync(kFull, lane < a.nranks && kq > a.K);
     if (truncated) {
-      if (lane == 0) a.fb_rows[atomicAdd(a.fb_count, 1)] = (int32_t)row;
+      // left for the exact full-row path; its loss share starts at 0
+      if (lane == 0) {
+        a.fb_rows[atomicAdd(a.fb_count, 1)] = (int32_t)row;
+        if (a.loss_part) a.loss_part[row] = 0.0f;
+        if (a.kappa) a.kappa[row] = 0;
+        if (a.H) a.H[row] = CUDART_NAN_F;
+      }
       continue;
     }
 

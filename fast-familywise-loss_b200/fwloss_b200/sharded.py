@@ -18,7 +18,7 @@ q's own support (usually a handful of entries).  Per step:
 Rows where a shard's own support exceeds K entries (near-constant rows) are
 listed by step 3 and solved exactly from their full rows (gathered for those
 rows only, then the unsharded fused kernel); reading that count is one 4-byte
-device-to-host copy per step.
+device-to-host copy per step, issued after the step's other work is queued.
 """
 import torch
 import torch.distributed as dist
@@ -54,17 +54,23 @@ def scan_phase(z_local, K=DEFAULT_K):
     return ext().shard_scan(z_local, K)
 
 
-def solve_phase(gathered, z_local, target, col_start, rank, scale, grad, local_idx, all_gather):
-    """Step 3 (and the exact path for listed rows) on one rank; `all_gather(x)`
-    returns the rank-major stack of x over all ranks.  Returns (H, kappa,
-    loss_part, fallback row count); grad is patched in place."""
-    H, kappa, loss_part, fb_rows, fb_count = ext().shard_solve(gathered, rank, list(col_start), z_local, target,
-                                                               float(scale), grad, local_idx)
-    nfb = int(fb_count.item())  # identical on all ranks (computed from the same gathered data)
+def solve_phase(gathered, z_local, target, col_start, rank, scale, grad, local_idx):
+    """Step 3 on one rank.  Returns (H, kappa, loss_part, fb_rows, fb_count);
+    grad is patched in place; rows listed in fb_rows[:fb_count] are not solved
+    yet (finish_rows)."""
+    return ext().shard_solve(gathered, rank, list(col_start), z_local, target, float(scale), grad, local_idx)
+
+
+def finish_rows(fb_rows, fb_count, z_local, target, col_start, rank, scale, all_gather, grad, H, kappa,
+                loss_part):
+    """Exact path for the rows step 3 could not solve.  Reads the row count
+    (one 4-byte device-to-host copy; identical on all ranks because it is
+    computed from the same gathered data).  Returns the count."""
+    nfb = int(fb_count.item())
     if nfb:
         rows = fb_rows[:nfb].long().sort().values
         _solve_full_rows(z_local, target, col_start, rank, scale, all_gather, rows, grad, H, kappa, loss_part)
-    return H, kappa, loss_part, nfb
+    return nfb
 
 
 def sharded_step(z_local, target, col_start, rank, scale, all_gather, K=DEFAULT_K):
@@ -72,9 +78,29 @@ def sharded_step(z_local, target, col_start, rank, scale, all_gather, K=DEFAULT_
     where loss_part[r] is row r's loss on the rank that owns the label and 0
     elsewhere."""
     grad, summary, local_idx = scan_phase(z_local, K)
-    H, kappa, loss_part, _ = solve_phase(all_gather(summary), z_local, target, col_start, rank, scale, grad,
-                                         local_idx, all_gather)
+    H, kappa, loss_part, fb_rows, fb_count = solve_phase(all_gather(summary), z_local, target, col_start, rank,
+                                                         scale, grad, local_idx)
+    finish_rows(fb_rows, fb_count, z_local, target, col_start, rank, scale, all_gather, grad, H, kappa, loss_part)
     return grad, H, kappa, loss_part
+
+
+def sharded_loss_step(z_local, target, col_start, rank, scale, all_gather, all_reduce, K=DEFAULT_K):
+    """One full step for one rank, with the host read of the exact-path row
+    count placed after all common-path work is queued: (grad shard, global
+    loss sum * scale as a 0-d tensor)."""
+    fw = ext()
+    grad, summary, local_idx = scan_phase(z_local, K)
+    H, kappa, loss_part, fb_rows, fb_count = solve_phase(all_gather(summary), z_local, target, col_start, rank,
+                                                         scale, grad, local_idx)
+    loss = all_reduce(fw.loss_reduce(loss_part, float(scale)).reshape(1))
+    nfb = int(fb_count.item())
+    if nfb:  # rare: solve those rows from their full rows, then add their losses
+        rows = fb_rows[:nfb].long().sort().values
+        before = loss_part[rows].clone()
+        _solve_full_rows(z_local, target, col_start, rank, scale, all_gather, rows, grad, H, kappa, loss_part)
+        corr = ((loss_part[rows] - before).double().sum() * scale).float().reshape(1)
+        loss = loss + all_reduce(corr)
+    return grad, loss.reshape(())
 
 
 def _solve_full_rows(z_local, target, col_start, rank, scale, all_gather, rows, grad, H, kappa, loss_part):
@@ -101,11 +127,11 @@ class _ClassSharded(torch.autograd.Function):
     @staticmethod
     def forward(ctx, z_local, target, col_start, scale, group, K):
         rank = dist.get_rank(group)
-        grad, H, kappa, loss_part = sharded_step(z_local.detach(), target, col_start, rank, scale,
-                                                 lambda x: _nccl_all_gather(x, group), K)
+        grad, loss = sharded_loss_step(z_local.detach(), target, col_start, rank, scale,
+                                       lambda x: _nccl_all_gather(x, group),
+                                       lambda t: _nccl_all_reduce(t, group), K)
         ctx.grad = grad
-        local = ext().loss_reduce(loss_part, float(scale))
-        return _nccl_all_reduce(local.reshape(1), group).reshape(())
+        return loss
 
     @staticmethod
     def backward(ctx, g):

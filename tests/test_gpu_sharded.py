@@ -16,7 +16,7 @@ import torch
 
 import cases
 from fwloss_b200 import capi, workloads
-from fwloss_b200.sharded import _solve_full_rows, even_col_start, scan_phase
+from fwloss_b200.sharded import _solve_full_rows, even_col_start, scan_phase, solve_phase
 from fwloss_b200._native import ext
 from oracle import fw_oracle as O
 
@@ -33,8 +33,8 @@ def emulate(z, y, col_start, scale, K):
     out = []
     for q in range(world):
         grad, _, local_idx = scans[q]
-        H, kappa, loss_part, fb_rows, fb_count = ext().shard_solve(gathered, q, list(col_start), shards[q], y,
-                                                                   float(scale), grad, local_idx)
+        H, kappa, loss_part, fb_rows, fb_count = solve_phase(gathered, shards[q], y, col_start, q, scale, grad,
+                                                             local_idx)
         nfb = int(fb_count.item())
         if nfb:
             rows = fb_rows[:nfb].long().sort().values
