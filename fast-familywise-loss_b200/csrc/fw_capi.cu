@@ -18,6 +18,7 @@
 #include "../../include/fwloss_b200.h"
 #include "fw_aux.cuh"
 #include "fw_device.cuh"
+#include "fw_lmhead.cuh"
 #include "fw_shard.cuh"
 #include "fw_stream_tier.cuh"
 #include "fw_warp_tier.cuh"
@@ -304,13 +305,13 @@ int fw_shard_scan(const float* z, int64_t B, int64_t C_local, int64_t ld, int K,
                   int32_t* summary, int32_t* local_idx, void* stream) {
   if (int rc = check_shape(B, C_local, ld)) return rc;
   if (K < 1 || K > kShardMaxK) return FWB_E_CAPACITY;
-  if (B > 0 && (!z || !grad || !summary || !local_idx)) return FWB_E_POINTER;
+  if (B > 0 && (!z || !summary || !local_idx)) return FWB_E_POINTER;  // grad optional
   RowArgs a = base_args(z, nullptr, B, C_local, ld, nullptr, nullptr, nullptr, nullptr);
   a.grad = grad;
   a.shard_sum = summary;
   a.shard_idx = local_idx;
   a.shard_k = K;
-  const bool vec = aligned16(z) && aligned16(grad) && (ld % 4 == 0);
+  const bool vec = aligned16(z) && (grad == nullptr || aligned16(grad)) && (ld % 4 == 0);
   return run_rows<float, kOutShard>(a, static_cast<cudaStream_t>(stream), vec);
 }
 
@@ -353,6 +354,82 @@ int fw_shard_solve(const int32_t* gathered, int nranks, int rank, const int64_t*
   const int warps = kShardSolveThreads / 32;
   return launch_status(launch(fw_shard_solve_kernel, dim3(aux_grid(B, warps)), dim3(kShardSolveThreads), 1,
                               st, a));
+}
+
+int fw_label_logits(const float* z, int64_t B, int64_t C, int64_t ld, const int64_t* y, int64_t c0,
+                    float* zy, void* stream) {
+  if (int rc = check_shape(B, C, ld)) return rc;
+  if (B == 0) return FWB_OK;
+  if (!z || !y || !zy) return FWB_E_POINTER;
+  const int threads = 256;
+  const int64_t blocks = (B + threads - 1) / threads;
+  return launch_status(launch(fw_label_logit_kernel, dim3((unsigned)(blocks < 4096 ? blocks : 4096)),
+                              dim3(threads), 1, static_cast<cudaStream_t>(stream), z, B, C, ld, y, c0, zy));
+}
+
+int fw_chunks_solve(const int32_t* summaries, const int32_t* local_idx, int nchunks,
+                    const int64_t* col_start, int64_t B, int K, const float* zy, const int64_t* y,
+                    float* H, int32_t* kappa, float* loss, int32_t* sup_cols, int32_t* fb_rows,
+                    int32_t* fb_count, int32_t* status, void* stream) {
+  if (nchunks < 1 || nchunks > kMaxShards || !col_start || B < 0) return FWB_E_SHAPE;
+  if (K < 1 || K > kShardMaxK || nchunks * K > kShardListCap) return FWB_E_CAPACITY;
+  if (col_start[0] != 0) return FWB_E_SHAPE;
+  for (int q = 0; q < nchunks; ++q)
+    if (col_start[q + 1] <= col_start[q]) return FWB_E_SHAPE;
+  if (!fb_count) return FWB_E_POINTER;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(fb_count, 0, sizeof(int32_t), st) != cudaSuccess) return FWB_E_LAUNCH;
+  if (B == 0) return FWB_OK;
+  if (!summaries || !local_idx || !zy || !y || !kappa || !sup_cols || !fb_rows) return FWB_E_POINTER;
+  ChunkSolveArgs a = {};
+  a.summaries = summaries;
+  a.local_idx = local_idx;
+  a.nchunks = nchunks;
+  a.K = K;
+  a.B = B;
+  for (int q = 0; q <= nchunks; ++q) a.col_start[q] = col_start[q];
+  a.zy = zy;
+  a.y = y;
+  a.H = H;
+  a.kappa = kappa;
+  a.loss = loss;
+  a.sup_cols = sup_cols;
+  a.fb_rows = fb_rows;
+  a.fb_count = fb_count;
+  a.status = status;
+  const int warps = kShardSolveThreads / 32;
+  return launch_status(launch(fw_chunks_solve_kernel, dim3(aux_grid(B, warps)), dim3(kShardSolveThreads), 1,
+                              st, a));
+}
+
+int fw_sparse_grad_hidden(int dtype, const void* weight, int64_t C, int64_t D, const int32_t* sup_cols,
+                          int S, const int32_t* kappa, const int64_t* y, int64_t B, float scale,
+                          const float* grad_output, int per_row, void* dhidden, void* stream) {
+  if (dtype != FWB_DTYPE_F32 && dtype != FWB_DTYPE_BF16) return FWB_E_DTYPE;
+  if (B < 0 || C < 1 || D < 1 || S < 1) return FWB_E_SHAPE;
+  if (B == 0) return FWB_OK;
+  if (!weight || !sup_cols || !kappa || !y || !grad_output || !dhidden) return FWB_E_POINTER;
+  SparseGradArgs a = {weight, dhidden, B, C, D, sup_cols, S, kappa, y, scale, grad_output, per_row};
+  const dim3 grid(aux_grid(B, 1)), block(kSparseThreads);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return launch_status(dtype == FWB_DTYPE_BF16
+                           ? launch(fw_sparse_dhidden_kernel<__nv_bfloat16>, grid, block, 1, st, a)
+                           : launch(fw_sparse_dhidden_kernel<float>, grid, block, 1, st, a));
+}
+
+int fw_sparse_grad_weight(int dtype, const void* hidden, int64_t B, int64_t D, const int32_t* sup_cols,
+                          int S, const int32_t* kappa, const int64_t* y, int64_t C, float scale,
+                          const float* grad_output, int per_row, float* dweight, void* stream) {
+  if (dtype != FWB_DTYPE_F32 && dtype != FWB_DTYPE_BF16) return FWB_E_DTYPE;
+  if (B < 0 || C < 1 || D < 1 || S < 1) return FWB_E_SHAPE;
+  if (B == 0) return FWB_OK;
+  if (!hidden || !sup_cols || !kappa || !y || !grad_output || !dweight) return FWB_E_POINTER;
+  SparseGradArgs a = {hidden, dweight, B, C, D, sup_cols, S, kappa, y, scale, grad_output, per_row};
+  const dim3 grid(aux_grid(B, 1)), block(kSparseThreads);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return launch_status(dtype == FWB_DTYPE_BF16
+                           ? launch(fw_sparse_dweight_kernel<__nv_bfloat16>, grid, block, 1, st, a)
+                           : launch(fw_sparse_dweight_kernel<float>, grid, block, 1, st, a));
 }
 
 int fw_loss_reduce(const float* loss, int64_t B, double scale, float* out, void* stream) {

@@ -244,7 +244,8 @@ __global__ void __launch_bounds__(kST)
   bool ovf = false;
   float* lz = s.lz[w];
   int* li = s.li[w];
-  T* gr = kZeroFill ? static_cast<T*>(a.grad) + row * a.ld : nullptr;
+  // kOutShard without a gradient shard (a.grad == null) only writes summaries
+  T* gr = (kZeroFill && a.grad) ? static_cast<T*>(a.grad) + row * a.ld : nullptr;
   uint8_t* mr = (OUT == kOutMask) ? a.mask + row * C : nullptr;
 
   for (int64_t base = g.i0; base < g.i1; base += (int64_t)kST * IPT) {
@@ -267,7 +268,7 @@ __global__ void __launch_bounds__(kST)
     for (int u = 0; u < IPT; ++u) {
       const int64_t it = base + (int64_t)u * kST + tid;
       if (it < g.i1) {
-        if (kZeroFill) {
+        if (kZeroFill && (OUT == kOutGrad || gr != nullptr)) {
           if (VEC)
             *reinterpret_cast<uint4*>(gr + W * it) = make_uint4(0u, 0u, 0u, 0u);
           else
@@ -309,7 +310,7 @@ __global__ void __launch_bounds__(kST)
     const bool in = c < C;
     const float x = in ? ld_elem(zr + c) : -CUDART_INF_F;
     if (in) {
-      if (kZeroFill) st_elem(gr + c, 0.0f);
+      if (kZeroFill && (OUT == kOutGrad || gr != nullptr)) st_elem(gr + c, 0.0f);
       if (OUT == kOutMask) mr[c] = 0;
     }
     run = max_nan(run, warp_max_nan(x));

@@ -14,7 +14,9 @@
 //   * candidate_buffer/indices rows hold exactly the support (kappa entries),
 //     so fw_backward needs no zero-initialised [N,K] buffer.
 // Extra functions used by the autograd layer (fwloss_b200 package):
-//   fused_fwd_bwd, scale_grad, loss_reduce, shard_scan, shard_solve.
+//   fused_fwd_bwd, scale_grad, loss_reduce, shard_scan, shard_solve, and the
+//   LM-head pieces shard_scan_into, label_logits, chunks_solve,
+//   sparse_grad_hidden, sparse_grad_weight.
 #include <torch/extension.h>
 
 #include <ATen/cuda/CUDAContext.h>
@@ -301,6 +303,102 @@ std::vector<torch::Tensor> shard_solve(torch::Tensor gathered, int64_t rank, std
   return {H, kappa, loss_part, fb_rows, fb_count};
 }
 
+// Summaries of one logit chunk written into given buffers (no gradient shard).
+void shard_scan_into(torch::Tensor z_chunk, int64_t K, torch::Tensor summary, torch::Tensor local_idx) {
+  check_logits(z_chunk);
+  const c10::cuda::CUDAGuard guard(z_chunk.device());
+  const int64_t N = z_chunk.size(0), C = z_chunk.size(1);
+  int64_t ld = C;
+  auto z = rows_view(z_chunk, &ld);
+  TORCH_CHECK(summary.is_contiguous() && summary.scalar_type() == torch::kInt32 && summary.numel() == N * (4 + K),
+              "summary must be contiguous int32 [B, 4 + K]");
+  TORCH_CHECK(local_idx.is_contiguous() && local_idx.scalar_type() == torch::kInt32 && local_idx.numel() == N * K,
+              "local_idx must be contiguous int32 [B, K]");
+  check_rc(fw_shard_scan(z.data_ptr<float>(), N, C, ld, (int)K, nullptr, summary.data_ptr<int32_t>(),
+                         local_idx.data_ptr<int32_t>(), cur_stream()),
+           "fw_shard_scan");
+}
+
+void label_logits(torch::Tensor z_chunk, torch::Tensor targets, int64_t c0, torch::Tensor zy) {
+  check_logits(z_chunk);
+  const c10::cuda::CUDAGuard guard(z_chunk.device());
+  const int64_t N = z_chunk.size(0), C = z_chunk.size(1);
+  check_targets(targets, N, z_chunk);
+  TORCH_CHECK(zy.is_cuda() && zy.scalar_type() == torch::kFloat32 && zy.numel() == N && zy.is_contiguous(),
+              "zy must be a contiguous float32 [B] tensor");
+  int64_t ld = C;
+  auto z = rows_view(z_chunk, &ld);
+  auto y = targets.contiguous();
+  check_rc(fw_label_logits(z.data_ptr<float>(), N, C, ld, y.data_ptr<int64_t>(), c0, zy.data_ptr<float>(),
+                           cur_stream()),
+           "fw_label_logits");
+}
+
+// (H, kappa, loss, sup_cols, fb_rows, fb_count) from the chunk summaries.
+std::vector<torch::Tensor> chunks_solve(torch::Tensor summaries, torch::Tensor local_idx,
+                                        std::vector<int64_t> col_start, torch::Tensor zy, torch::Tensor targets,
+                                        c10::optional<torch::Tensor> status) {
+  TORCH_CHECK(summaries.is_cuda() && summaries.scalar_type() == torch::kInt32 && summaries.dim() == 3 &&
+                  summaries.is_contiguous(),
+              "summaries must be contiguous int32 [nchunks, B, 4 + K]");
+  const c10::cuda::CUDAGuard guard(summaries.device());
+  const int64_t n = summaries.size(0), B = summaries.size(1), K = summaries.size(2) - 4;
+  TORCH_CHECK((int64_t)col_start.size() == n + 1, "col_start must have nchunks + 1 entries");
+  TORCH_CHECK(local_idx.is_contiguous() && local_idx.numel() == n * B * K, "local_idx must be [nchunks, B, K]");
+  check_targets(targets, B, summaries);
+  auto y = targets.contiguous();
+  auto opt = summaries.options();
+  auto H = torch::empty({B}, opt.dtype(torch::kFloat32));
+  auto kappa = torch::empty({B}, opt);
+  auto loss = torch::empty({B}, opt.dtype(torch::kFloat32));
+  auto sup = torch::empty({B, n * K}, opt);
+  auto fb_rows = torch::empty({B > 0 ? B : 1}, opt);
+  auto fb_count = torch::empty({1}, opt);
+  int32_t* st = nullptr;
+  if (status.has_value()) st = status->data_ptr<int32_t>();
+  check_rc(fw_chunks_solve(summaries.data_ptr<int32_t>(), local_idx.data_ptr<int32_t>(), (int)n, col_start.data(), B,
+                           (int)K, zy.data_ptr<float>(), y.data_ptr<int64_t>(), H.data_ptr<float>(),
+                           kappa.data_ptr<int32_t>(), loss.data_ptr<float>(), sup.data_ptr<int32_t>(),
+                           fb_rows.data_ptr<int32_t>(), fb_count.data_ptr<int32_t>(), st, cur_stream()),
+           "fw_chunks_solve");
+  return {H, kappa, loss, sup, fb_rows, fb_count};
+}
+
+int lm_dtype(const torch::Tensor& t) {
+  TORCH_CHECK(t.scalar_type() == torch::kFloat32 || t.scalar_type() == torch::kBFloat16,
+              "LM-head tensors must be float32 or bfloat16");
+  return t.scalar_type() == torch::kBFloat16 ? FWB_DTYPE_BF16 : FWB_DTYPE_F32;
+}
+
+torch::Tensor sparse_grad_hidden(torch::Tensor weight, torch::Tensor sup_cols, torch::Tensor kappa,
+                                 torch::Tensor targets, double scale, torch::Tensor grad_output, bool per_row) {
+  TORCH_CHECK(weight.is_cuda() && weight.dim() == 2 && weight.is_contiguous(), "weight must be contiguous [C, D]");
+  const c10::cuda::CUDAGuard guard(weight.device());
+  const int64_t B = kappa.numel();
+  auto dH = torch::empty({B, weight.size(1)}, weight.options());
+  auto go = grad_output.to(weight.device(), torch::kFloat32).contiguous();
+  check_rc(fw_sparse_grad_hidden(lm_dtype(weight), weight.data_ptr(), weight.size(0), weight.size(1),
+                                 sup_cols.data_ptr<int32_t>(), (int)sup_cols.size(1), kappa.data_ptr<int32_t>(),
+                                 targets.data_ptr<int64_t>(), B, (float)scale, go.data_ptr<float>(), per_row ? 1 : 0,
+                                 dH.data_ptr(), cur_stream()),
+           "fw_sparse_grad_hidden");
+  return dH;
+}
+
+void sparse_grad_weight(torch::Tensor hidden, torch::Tensor sup_cols, torch::Tensor kappa, torch::Tensor targets,
+                        double scale, torch::Tensor grad_output, bool per_row, torch::Tensor dweight) {
+  TORCH_CHECK(hidden.is_cuda() && hidden.dim() == 2 && hidden.is_contiguous(), "hidden must be contiguous [B, D]");
+  TORCH_CHECK(dweight.scalar_type() == torch::kFloat32 && dweight.is_contiguous() && dweight.size(1) == hidden.size(1),
+              "dweight must be a contiguous float32 [C, D] accumulator");
+  const c10::cuda::CUDAGuard guard(hidden.device());
+  auto go = grad_output.to(hidden.device(), torch::kFloat32).contiguous();
+  check_rc(fw_sparse_grad_weight(lm_dtype(hidden), hidden.data_ptr(), hidden.size(0), hidden.size(1),
+                                 sup_cols.data_ptr<int32_t>(), (int)sup_cols.size(1), kappa.data_ptr<int32_t>(),
+                                 targets.data_ptr<int64_t>(), dweight.size(0), (float)scale, go.data_ptr<float>(),
+                                 per_row ? 1 : 0, dweight.data_ptr<float>(), cur_stream()),
+           "fw_sparse_grad_weight");
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "B200 (sm_100a) Familywise loss: drop-in for the fw_radix_cuda module";
   m.def("fw_forward", &fw_forward, "FW forward (support as candidate lists)");
@@ -312,6 +410,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("scale_grad", &scale_grad, "in-place grad scaling by a device-side grad_output");
   m.def("loss_reduce", &loss_reduce, "deterministic scale * sum(losses)");
   m.def("shard_scan", &shard_scan, "class-sharded step 1: local solve, zero gradient shard, summaries");
+  m.def("shard_scan_into", &shard_scan_into, "summaries of one logit chunk into given buffers");
+  m.def("label_logits", &label_logits, "zy[r] = chunk[r, y[r] - c0] for labels inside the chunk");
+  m.def("chunks_solve", &chunks_solve, "LM head: combine chunk summaries",
+        py::arg("summaries"), py::arg("local_idx"), py::arg("col_start"), py::arg("zy"), py::arg("targets"),
+        py::arg("status") = py::none());
+  m.def("sparse_grad_hidden", &sparse_grad_hidden, "LM head backward: dhidden from the sparse logit gradient");
+  m.def("sparse_grad_weight", &sparse_grad_weight, "LM head backward: dweight += (fp32 accumulator)");
   m.def("shard_solve", &shard_solve, "class-sharded step 3: global solve from gathered summaries",
         py::arg("gathered"), py::arg("rank"), py::arg("col_start"), py::arg("z_local"), py::arg("targets"),
         py::arg("grad_scale"), py::arg("grad"), py::arg("local_idx"), py::arg("status") = py::none());

@@ -132,11 +132,13 @@ __device__ __forceinline__ void warp_tier_nonfinite(const RowArgs& a, int64_t ro
       a.cand_idx[row * a.C] = jstar;
       if (a.cand_count) a.cand_count[row] = 1;
     }
-  } else {  // kOutShard: zero gradient shard, summary of a non-finite row
-    T* gr = static_cast<T*>(a.grad) + row * a.ld;
-    const float zero[Elem<T>::kEPS] = {};
+  } else {  // kOutShard: zero gradient shard (if any), summary of a non-finite row
+    if (a.grad) {
+      T* gr = static_cast<T*>(a.grad) + row * a.ld;
+      const float zero[Elem<T>::kEPS] = {};
 #pragma unroll
-    for (int i = 0; i < NS; ++i) warp_tier_store_slot<T, G, VEC, false>(gr, i, li, C, zero);
+      for (int i = 0; i < NS; ++i) warp_tier_store_slot<T, G, VEC, false>(gr, i, li, C, zero);
+    }
     if (li == 0) {
       int32_t* rec = a.shard_sum + row * (int64_t)(kShardHeader + a.shard_k);
       rec[0] = __float_as_int(m);
@@ -302,11 +304,13 @@ __global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS * El
         warp_tier_store_mask<G, VEC, FULLV>(mr, i, li, C, a.mask_vec, b);
       }
     } else if (OUT == kOutShard) {
-      // zero gradient shard; the support goes to the summary record
-      T* gr = static_cast<T*>(a.grad) + row * a.ld;
-      const float zero[EPS] = {};
+      // zero gradient shard (if any); the support goes to the summary record
+      if (a.grad) {
+        T* gr = static_cast<T*>(a.grad) + row * a.ld;
+        const float zero[EPS] = {};
 #pragma unroll
-      for (int i = 0; i < NS; ++i) warp_tier_store_slot<T, G, VEC, FULLV>(gr, i, li, C, zero);
+        for (int i = 0; i < NS; ++i) warp_tier_store_slot<T, G, VEC, FULLV>(gr, i, li, C, zero);
+      }
       int cnt = 0;
 #pragma unroll
       for (int s = 0; s < NV; ++s) cnt += (v[s] > Hf) ? 1 : 0;

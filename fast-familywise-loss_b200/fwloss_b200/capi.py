@@ -37,6 +37,13 @@ _SIGS = {
 _SIGS["fw_shard_scan"] = ([_P, _I64, _I64, _I64, ctypes.c_int, _P, _P, _P, _P], ctypes.c_int)
 _SIGS["fw_shard_solve"] = ([_P, ctypes.c_int, ctypes.c_int, _P, _I64, ctypes.c_int, _P, _I64, _P,
                            ctypes.c_float, _P, _P, _P, _P, _P, _P, _P, _P, _P], ctypes.c_int)
+_SIGS["fw_label_logits"] = ([_P, _I64, _I64, _I64, _P, _I64, _P, _P], ctypes.c_int)
+_SIGS["fw_chunks_solve"] = ([_P, _P, ctypes.c_int, _P, _I64, ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                            _P], ctypes.c_int)
+_SIGS["fw_sparse_grad_hidden"] = ([ctypes.c_int, _P, _I64, _I64, _P, ctypes.c_int, _P, _P, _I64, ctypes.c_float,
+                                  _P, ctypes.c_int, _P, _P], ctypes.c_int)
+_SIGS["fw_sparse_grad_weight"] = ([ctypes.c_int, _P, _I64, _I64, _P, ctypes.c_int, _P, _P, _I64, ctypes.c_float,
+                                  _P, ctypes.c_int, _P, _P], ctypes.c_int)
 DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 
 EXPORTED = tuple(_SIGS)

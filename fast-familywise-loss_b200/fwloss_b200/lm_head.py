@@ -1,0 +1,117 @@
+"""FW loss on top of an LM head without materialising [B, C] logits or their
+gradient.
+
+    from fwloss_b200.lm_head import fw_lm_head_loss
+    loss = fw_lm_head_loss(hidden, weight, target)     # hidden [B, D], weight [C, D]
+    loss.backward()                                    # hidden.grad, weight.grad
+
+Forward: the logits are produced one column chunk at a time by the GEMM
+(cuBLAS through torch.mm, fp32 output; bf16 inputs are accumulated in fp32)
+and each chunk is reduced at once to per-row summaries by the fused kernel
+(chunk max, the chunk's own support, up to K values) -- only one chunk of
+logits exists at a time.  The chunk summaries are then combined per row
+(fw_chunks_solve), which gives H, kappa, the loss and the support columns.
+
+Backward: the logit gradient of a row has kappa + 1 non-zeros
+(scale / kappa on the support, -scale at the label), so
+dhidden = G W and dweight = G^T hidden become gathers and scatter-adds of
+kappa + 1 rows per sample (fw_sparse_grad_hidden / fw_sparse_grad_weight)
+instead of two dense [B, C] x [C, D] GEMMs.  dweight is accumulated in fp32
+with atomics (the order of the additions is not fixed).
+
+Rows where a chunk's own support exceeds K entries (near-constant logits) are
+solved exactly from their full logit rows, and their gradient rows are
+applied densely; counting them costs one 4-byte device-to-host read per step.
+"""
+import torch
+
+from ._native import ext
+from .sharded import even_col_start
+
+DEFAULT_K = 16
+
+
+def _logits_chunk(hidden, w_chunk):
+    if hidden.dtype == torch.float32:
+        return torch.mm(hidden, w_chunk.t())
+    return torch.mm(hidden, w_chunk.t(), out_dtype=torch.float32)
+
+
+def _full_logits(hidden_rows, weight):
+    return _logits_chunk(hidden_rows, weight)
+
+
+class _FWLMHead(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, hidden, weight, target, scale, nchunks, K):
+        fw = ext()
+        B = hidden.shape[0]
+        C = weight.shape[0]
+        col_start = even_col_start(C, nchunks)
+        dev = hidden.device
+        summaries = torch.empty((nchunks, B, 4 + K), dtype=torch.int32, device=dev)
+        local_idx = torch.empty((nchunks, B, K), dtype=torch.int32, device=dev)
+        zy = torch.empty(B, dtype=torch.float32, device=dev)
+        for q in range(nchunks):
+            c0, c1 = col_start[q], col_start[q + 1]
+            z = _logits_chunk(hidden, weight[c0:c1])
+            fw.shard_scan_into(z, K, summaries[q], local_idx[q])
+            fw.label_logits(z, target, c0, zy)
+            del z
+        H, kappa, loss_rows, sup_cols, fb_rows, fb_count = fw.chunks_solve(summaries, local_idx, col_start, zy, target)
+        nfb = int(fb_count.item())
+        rows = g_rows = None
+        if nfb:
+            rows = fb_rows[:nfb].long().sort().values
+            zf = _full_logits(hidden[rows], weight)
+            g_rows, h, l, k = fw.fused_fwd_bwd(zf, target[rows], 1.0, None)
+            loss_rows[rows] = l
+            H[rows] = h
+        ctx.save_for_backward(hidden, weight, target, kappa, sup_cols)
+        ctx.rows, ctx.g_rows, ctx.scale = rows, g_rows, float(scale)
+        out = fw.loss_reduce(loss_rows, float(scale))
+        return out if hidden.dtype == torch.float32 else out.to(hidden.dtype)
+
+    @staticmethod
+    def backward(ctx, g):
+        fw = ext()
+        hidden, weight, target, kappa, sup_cols = ctx.saved_tensors
+        go = g.float().reshape(1)
+        dH = dW = None
+        if ctx.needs_input_grad[0]:
+            dH = fw.sparse_grad_hidden(weight, sup_cols, kappa, target, ctx.scale, go, False)
+        if ctx.needs_input_grad[1]:
+            dW32 = torch.zeros(weight.shape, dtype=torch.float32, device=weight.device)
+            fw.sparse_grad_weight(hidden, sup_cols, kappa, target, ctx.scale, go, False, dW32)
+        if ctx.rows is not None:  # rows solved from their full logits: dense gradient rows
+            gr = ctx.g_rows * (go * ctx.scale)
+            if dH is not None:
+                dH[ctx.rows] = (gr @ weight.float()).to(dH.dtype)
+            if ctx.needs_input_grad[1]:
+                dW32 += gr.t() @ hidden[ctx.rows].float()
+        if ctx.needs_input_grad[1]:
+            dW = dW32 if weight.dtype == torch.float32 else dW32.to(weight.dtype)
+        return dH, dW, None, None, None, None
+
+
+def fw_lm_head_loss(hidden, weight, target, reduction="mean", nchunks=None, K=DEFAULT_K):
+    """Mean/sum FW loss of logits = hidden @ weight^T.
+
+    hidden [B, D] and weight [C, D]: CUDA, both float32 or both bfloat16;
+    target [B] int64.  `nchunks` column chunks (default: chunks of ~16k
+    classes, at most 16) bound the logit memory to B x C / nchunks fp32."""
+    if reduction not in ("mean", "sum"):
+        raise ValueError(f"Invalid reduction mode: {reduction}")
+    if not (hidden.is_cuda and weight.is_cuda and hidden.dim() == 2 and weight.dim() == 2):
+        raise TypeError("fw_lm_head_loss: hidden [B, D] and weight [C, D] must be CUDA matrices")
+    if hidden.dtype != weight.dtype or hidden.dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError("fw_lm_head_loss: hidden and weight must both be float32 or both bfloat16")
+    if hidden.shape[1] != weight.shape[1]:
+        raise ValueError("fw_lm_head_loss: hidden and weight disagree on D")
+    C = weight.shape[0]
+    if nchunks is None:
+        nchunks = max(1, min(16, -(-C // 16384)))
+    nchunks = max(1, min(int(nchunks), C, 16, 256 // int(K)))
+    B = hidden.shape[0]
+    scale = (1.0 / B if B else float("nan")) if reduction == "mean" else 1.0
+    return _FWLMHead.apply(hidden.contiguous(), weight.contiguous(), target, scale, nchunks, int(K))

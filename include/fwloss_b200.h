@@ -166,7 +166,7 @@ FWB_API int fw_scale_grad_typed(int dtype, void* grad, const float* grad_output,
  *
  * Step 1, on every rank: fw_shard_scan solves each row of the local shard
  * [B, C_local] on its own, zero-fills the local gradient shard `grad`
- * (row stride ld) and writes a summary record per row into
+ * (row stride ld; NULL: no gradient shard) and writes a summary record per row into
  * summary[B, 4 + K] (int32 words: local max as float bits, local support size
  * kappa_q, flags, first maximal column; then up to K support values as float
  * bits) and the support's local columns into local_idx[B, K].  1 <= K <= 64.
@@ -195,6 +195,52 @@ FWB_API int fw_shard_solve(const int32_t* gathered, int nranks, int rank,
                            const int32_t* local_idx, float* H, int32_t* kappa,
                            float* loss_part, int32_t* fb_rows, int32_t* fb_count,
                            int32_t* status, void* stream);
+
+/*
+ * LM head, logits = hidden [B, D] x weight [C, D]^T, without a resident
+ * [B, C] logit matrix.  No counterpart in the reference (it takes logits as
+ * input); the math is the reference's (reference_impl.py:11-26).
+ *
+ * The caller produces the logits one column chunk [col_start[q],
+ * col_start[q+1]) at a time (any GEMM) and, per chunk, calls
+ * fw_shard_scan(chunk, ..., grad = NULL, summary_q, local_idx_q) (summaries
+ * only) and fw_label_logits(chunk, ..., c0 = col_start[q], zy) (keeps the
+ * logit at the label).  fw_chunks_solve then combines the nchunks summaries
+ * (summaries [nchunks, B, 4 + K], local_idx [nchunks, B, K]; nchunks <= 16,
+ * nchunks * K <= 256) into H, kappa, loss and the support's columns
+ * sup_cols[B, nchunks * K] (first kappa entries of each row).  Rows whose chunk
+ * supports exceed K get kappa = 0 and are listed in fb_rows[0 .. *fb_count)
+ * for the caller's exact path.
+ *
+ * The logit gradient then has kappa + 1 non-zeros per row, so the LM-head
+ * backward is two sparse kernels instead of two dense GEMMs:
+ *   fw_sparse_grad_hidden:  dhidden[r] = g_r (sum_{j in supp} W[j] / kappa_r - W[y_r])
+ *   fw_sparse_grad_weight:  dweight[j] += g_r (hidden[r] / kappa_r, j in supp(r);
+ *                                          -hidden[r], j = y_r)   (fp32, atomics)
+ * with g_r = scale * grad_output[per_row ? r : 0]; rows with kappa 0 are
+ * skipped (dhidden row set to 0).  dtype: FWB_DTYPE_F32 or FWB_DTYPE_BF16 for
+ * weight / hidden / dhidden.
+ */
+FWB_API int fw_label_logits(const float* z, int64_t B, int64_t C, int64_t ld, const int64_t* y,
+                            int64_t c0, float* zy, void* stream);
+
+FWB_API int fw_chunks_solve(const int32_t* summaries, const int32_t* local_idx, int nchunks,
+                            const int64_t* col_start, int64_t B, int K, const float* zy,
+                            const int64_t* y, float* H, int32_t* kappa, float* loss,
+                            int32_t* sup_cols, int32_t* fb_rows, int32_t* fb_count,
+                            int32_t* status, void* stream);
+
+FWB_API int fw_sparse_grad_hidden(int dtype, const void* weight, int64_t C, int64_t D,
+                                  const int32_t* sup_cols, int S, const int32_t* kappa,
+                                  const int64_t* y, int64_t B, float scale,
+                                  const float* grad_output, int per_row, void* dhidden,
+                                  void* stream);
+
+FWB_API int fw_sparse_grad_weight(int dtype, const void* hidden, int64_t B, int64_t D,
+                                  const int32_t* sup_cols, int S, const int32_t* kappa,
+                                  const int64_t* y, int64_t C, float scale,
+                                  const float* grad_output, int per_row, float* dweight,
+                                  void* stream);
 
 /*
  * Deterministic (fixed-order, fp64) reduction out[0] = scale * sum_r loss[r].
