@@ -61,9 +61,11 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-graph", action="store_true", help="launch steps eagerly")
-    p.add_argument("--mode", default="rows", choices=["rows", "class-sharded"],
+    p.add_argument("--mode", default="rows", choices=["rows", "class-sharded", "lm-head"],
                    help="rows: rows sharded across GPUs (default); class-sharded: every GPU holds a "
-                        "column shard of every row (vocabulary-parallel), cfg4 shape")
+                        "column shard of every row (vocabulary-parallel), cfg4 shape; lm-head: "
+                        "logits = hidden @ weight^T (B=8192, D=4096, C=128256, bf16) with the chunked "
+                        "forward and sparse backward, next to the dense path")
     p.add_argument("--shard-k", type=int, default=32, help="class-sharded: support entries per shard summary")
     p.add_argument("--dtype", default="f32", choices=["f32", "bf16", "f16"],
                    help="logits/gradient element type (the metric is defined on f32)")
@@ -546,12 +548,71 @@ def run_class_sharded(a):
     return 0
 
 
+def run_lm_head(a):
+    """LM head + FW loss, fwd+bwd, one GPU: B=8192 rows, D=4096, C=128256
+    classes (cfg4's shape), bf16 hidden/weight.  Ours: logits chunk by chunk
+    (cuBLAS GEMM, fp32 out) reduced to summaries by the fused kernel, sparse
+    backward.  Dense: the bf16 GEMM's logits materialised, the fused FW kernel,
+    and autograd through the GEMM (two dense bf16 backward GEMMs)."""
+    import torch
+
+    from fwloss_b200 import familywise_loss
+    from fwloss_b200.lm_head import fw_lm_head_loss
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, D, C = 8192, 4096, 128256
+    g = torch.Generator(device=dev).manual_seed(4)
+    hidden = (torch.randn(B, D, generator=g, device=dev) / D ** 0.5 * 4).to(torch.bfloat16).requires_grad_(True)
+    weight = torch.randn(C, D, generator=g, device=dev).to(torch.bfloat16).requires_grad_(True)
+    target = torch.randint(0, C, (B,), generator=g, device=dev)
+
+    def ours():
+        hidden.grad = weight.grad = None
+        fw_lm_head_loss(hidden, weight, target).backward()
+
+    def dense():
+        hidden.grad = weight.grad = None
+        z = (hidden @ weight.t()).float()  # bf16 GEMM, logits materialised
+        familywise_loss(z, target).backward()
+
+    def timed(fn, steps):
+        for _ in range(a.warmup):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / steps
+
+    ms = timed(ours, a.steps)
+    ms_dense = timed(dense, max(1, a.steps // 2))
+    gemm_tflop = 2.0 * B * D * C / 1e12
+    print(json.dumps({
+        "metric": "LM head + FWLoss fwd+bwd rows/s (B=8192, D=4096, C=128256, bf16)",
+        "value": B / (ms / 1e3), "unit": UNIT, "n_gpus": 1, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "config": {"workload": "hidden [8192, 4096] x weight [128256, 4096]^T -> FW loss",
+                                        "forward_gemm_tflop": gemm_tflop},
+        "dense_path": {"ms_per_step": ms_dense, "value": B / (ms_dense / 1e3),
+                       "what": "bf16 GEMM, logits materialised (fp32), fused FW kernel, dense bf16 GEMM backward"},
+        "speedup_vs_dense": ms_dense / ms,
+        "forward_gemm_tflops_if_gemm_only": gemm_tflop / (ms / 1e3),
+    }), flush=True)
+    return 0
+
+
 def main():
     a = parse()
     if a.impl == "reference":
         return run_reference(a)
     if a.mode == "class-sharded":
         return run_class_sharded(a)
+    if a.mode == "lm-head":
+        return run_lm_head(a)
     return run_ours(a)
 
 

@@ -432,6 +432,35 @@ int fw_sparse_grad_weight(int dtype, const void* hidden, int64_t B, int64_t D, c
                            : launch(fw_sparse_dweight_kernel<float>, grid, block, 1, st, a));
 }
 
+int fw_weight_grad_keys(const int32_t* sup_cols, int S, const int32_t* kappa, const int64_t* y, int64_t B,
+                        int64_t C, int64_t* keys, void* stream) {
+  if (B < 0 || S < 1 || C < 1) return FWB_E_SHAPE;
+  if (B == 0) return FWB_OK;
+  if (!sup_cols || !kappa || !y || !keys) return FWB_E_POINTER;
+  const int64_t n = B * (int64_t)(S + 1);
+  const int threads = 256;
+  const int64_t blocks = (n + threads - 1) / threads;
+  return launch_status(launch(fw_weight_keys_kernel, dim3((unsigned)(blocks < 65535 ? blocks : 65535)),
+                              dim3(threads), 1, static_cast<cudaStream_t>(stream), sup_cols, S, kappa, y, B, C,
+                              keys));
+}
+
+int fw_segment_grad_weight(int dtype, const void* hidden, int64_t B, int64_t D, const int64_t* keys, int64_t nkeys,
+                           const int32_t* kappa, float scale, const float* grad_output, int per_row, void* dweight,
+                           void* stream) {
+  if (dtype != FWB_DTYPE_F32 && dtype != FWB_DTYPE_BF16) return FWB_E_DTYPE;
+  if (B < 0 || D < 1 || nkeys < 0) return FWB_E_SHAPE;
+  if (nkeys == 0) return FWB_OK;
+  if (!hidden || !keys || !kappa || !grad_output || !dweight) return FWB_E_POINTER;
+  SegmentGradArgs a = {hidden, dweight, B, D, keys, nkeys, kappa, scale, grad_output, per_row};
+  const int64_t windows = (nkeys + kSegmentWindow - 1) / kSegmentWindow;
+  const dim3 grid(aux_grid(windows, 1)), block(kSparseThreads);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return launch_status(dtype == FWB_DTYPE_BF16
+                           ? launch(fw_segment_dweight_kernel<__nv_bfloat16>, grid, block, 1, st, a)
+                           : launch(fw_segment_dweight_kernel<float>, grid, block, 1, st, a));
+}
+
 int fw_loss_reduce(const float* loss, int64_t B, double scale, float* out, void* stream) {
   if (B < 0) return FWB_E_SHAPE;
   if (!out || (B > 0 && !loss)) return FWB_E_POINTER;

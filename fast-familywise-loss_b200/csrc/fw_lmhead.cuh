@@ -229,4 +229,87 @@ __global__ void __launch_bounds__(kSparseThreads) fw_sparse_dweight_kernel(Spars
   }
 }
 
+// Deterministic dweight.  Contribution keys (j << 32) | (r << 1) | is_label,
+// one per non-zero of the logit gradient, are built at fixed shape
+// [B, S + 1] (unused slots get kNoKey, which sorts last), sorted, and each run
+// of equal column j is summed in key order by the CTA that owns the run's
+// first entry (no segment table, no data-dependent shapes):
+//   dweight[j] = sum g_r / kappa_r * hidden[r]  (support entries)
+//              + sum -g_r * hidden[r]           (label entries)
+// Columns without contributions are left to the caller (zero).
+constexpr int64_t kNoKey = 0x7fffffffffffffffLL;
+
+__global__ void fw_weight_keys_kernel(const int32_t* __restrict__ sup_cols, int S, const int32_t* __restrict__ kappa,
+                                      const int64_t* __restrict__ y, int64_t B, int64_t C, int64_t* __restrict__ keys) {
+  const int64_t n = B * (int64_t)(S + 1);
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = e / (S + 1);
+    const int k = (int)(e - r * (S + 1));
+    const int kap = kappa[r];
+    int64_t key = kNoKey;
+    if (kap > 0) {
+      if (k < kap) {
+        key = ((int64_t)sup_cols[r * S + k] << 32) | (r << 1);
+      } else if (k == S) {
+        const int64_t yl = y[r];
+        if (yl >= 0 && yl < C) key = (yl << 32) | (r << 1) | 1;
+      }
+    }
+    keys[e] = key;
+  }
+}
+
+struct SegmentGradArgs {
+  const void* hidden;        // [B, D] (T)
+  void* dweight;             // [C, D] (T)
+  int64_t B, D;
+  const int64_t* keys;       // sorted, kNoKey entries last
+  int64_t nkeys;
+  const int32_t* kappa;
+  float scale;
+  const float* go;
+  int per_row;
+};
+
+constexpr int kSegmentWindow = 32;  // sorted entries scanned for run starts per CTA step
+
+template <class T>
+__global__ void __launch_bounds__(kSparseThreads) fw_segment_dweight_kernel(SegmentGradArgs a) {
+  const T* Hd = static_cast<const T*>(a.hidden);
+  T* dW = static_cast<T*>(a.dweight);
+  for (int64_t w0 = (int64_t)blockIdx.x * kSegmentWindow; w0 < a.nkeys; w0 += (int64_t)gridDim.x * kSegmentWindow) {
+    const int64_t wend = min(w0 + kSegmentWindow, a.nkeys);
+    for (int64_t e0 = w0; e0 < wend; ++e0) {
+      const int64_t k0 = a.keys[e0];
+      if (k0 == kNoKey) return;  // the rest of the array is unused slots
+      const int64_t j = k0 >> 32;
+      if (e0 > 0 && (a.keys[e0 - 1] >> 32) == j) continue;  // not the first entry of its run
+      int64_t e1 = e0 + 1;
+      while (e1 < a.nkeys && a.keys[e1] != kNoKey && (a.keys[e1] >> 32) == j) ++e1;
+      for (int64_t d0 = 0; d0 < a.D; d0 += (int64_t)kSparseThreads * kSparseCols) {
+        float acc[kSparseCols];
+#pragma unroll
+        for (int i = 0; i < kSparseCols; ++i) acc[i] = 0.0f;
+        for (int64_t e = e0; e < e1; ++e) {
+          const int64_t key = a.keys[e];
+          const int64_t r = (key >> 1) & 0x7fffffffLL;
+          const float g = a.go[a.per_row ? r : 0] * a.scale;
+          const float coef = (key & 1) ? -g : (float)((double)g / (double)a.kappa[r]);
+          const T* hr = Hd + r * a.D;
+#pragma unroll
+          for (int i = 0; i < kSparseCols; ++i) {
+            const int64_t d = d0 + (int64_t)i * kSparseThreads + threadIdx.x;
+            if (d < a.D) acc[i] += coef * ld_elem(hr + d);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < kSparseCols; ++i) {
+          const int64_t d = d0 + (int64_t)i * kSparseThreads + threadIdx.x;
+          if (d < a.D) st_elem(dW + j * a.D + d, acc[i]);
+        }
+      }
+    }
+  }
+}
+
 }  // namespace fwb200

@@ -399,6 +399,35 @@ void sparse_grad_weight(torch::Tensor hidden, torch::Tensor sup_cols, torch::Ten
            "fw_sparse_grad_weight");
 }
 
+torch::Tensor weight_grad_keys(torch::Tensor sup_cols, torch::Tensor kappa, torch::Tensor targets, int64_t C) {
+  TORCH_CHECK(sup_cols.is_cuda() && sup_cols.scalar_type() == torch::kInt32 && sup_cols.dim() == 2 &&
+                  sup_cols.is_contiguous(),
+              "sup_cols must be contiguous int32 [B, S]");
+  const c10::cuda::CUDAGuard guard(sup_cols.device());
+  const int64_t B = sup_cols.size(0), S = sup_cols.size(1);
+  auto keys = torch::empty({B * (S + 1)}, sup_cols.options().dtype(torch::kLong));
+  check_rc(fw_weight_grad_keys(sup_cols.data_ptr<int32_t>(), (int)S, kappa.data_ptr<int32_t>(),
+                               targets.data_ptr<int64_t>(), B, C, keys.data_ptr<int64_t>(), cur_stream()),
+           "fw_weight_grad_keys");
+  return keys;
+}
+
+void segment_grad_weight(torch::Tensor hidden, torch::Tensor sorted_keys, torch::Tensor kappa, double scale,
+                         torch::Tensor grad_output, bool per_row, torch::Tensor dweight) {
+  TORCH_CHECK(hidden.is_cuda() && hidden.dim() == 2 && hidden.is_contiguous(), "hidden must be contiguous [B, D]");
+  TORCH_CHECK(dweight.scalar_type() == hidden.scalar_type() && dweight.is_contiguous() &&
+                  dweight.size(1) == hidden.size(1),
+              "dweight must be contiguous [C, D] of hidden's dtype");
+  TORCH_CHECK(sorted_keys.scalar_type() == torch::kLong && sorted_keys.is_contiguous(), "int64 sorted keys");
+  const c10::cuda::CUDAGuard guard(hidden.device());
+  auto go = grad_output.to(hidden.device(), torch::kFloat32).contiguous();
+  check_rc(fw_segment_grad_weight(lm_dtype(hidden), hidden.data_ptr(), hidden.size(0), hidden.size(1),
+                                  sorted_keys.data_ptr<int64_t>(), sorted_keys.numel(), kappa.data_ptr<int32_t>(),
+                                  (float)scale, go.data_ptr<float>(), per_row ? 1 : 0, dweight.data_ptr(),
+                                  cur_stream()),
+           "fw_segment_grad_weight");
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "B200 (sm_100a) Familywise loss: drop-in for the fw_radix_cuda module";
   m.def("fw_forward", &fw_forward, "FW forward (support as candidate lists)");
@@ -417,6 +446,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("status") = py::none());
   m.def("sparse_grad_hidden", &sparse_grad_hidden, "LM head backward: dhidden from the sparse logit gradient");
   m.def("sparse_grad_weight", &sparse_grad_weight, "LM head backward: dweight += (fp32 accumulator)");
+  m.def("weight_grad_keys", &weight_grad_keys, "LM head backward: contribution keys [B * (S + 1)]");
+  m.def("segment_grad_weight", &segment_grad_weight, "LM head backward: deterministic dweight rows from sorted keys");
   m.def("shard_solve", &shard_solve, "class-sharded step 3: global solve from gathered summaries",
         py::arg("gathered"), py::arg("rank"), py::arg("col_start"), py::arg("z_local"), py::arg("targets"),
         py::arg("grad_scale"), py::arg("grad"), py::arg("local_idx"), py::arg("status") = py::none());

@@ -44,6 +44,9 @@ _SIGS["fw_sparse_grad_hidden"] = ([ctypes.c_int, _P, _I64, _I64, _P, ctypes.c_in
                                   _P, ctypes.c_int, _P, _P], ctypes.c_int)
 _SIGS["fw_sparse_grad_weight"] = ([ctypes.c_int, _P, _I64, _I64, _P, ctypes.c_int, _P, _P, _I64, ctypes.c_float,
                                   _P, ctypes.c_int, _P, _P], ctypes.c_int)
+_SIGS["fw_weight_grad_keys"] = ([_P, ctypes.c_int, _P, _P, _I64, _I64, _P, _P], ctypes.c_int)
+_SIGS["fw_segment_grad_weight"] = ([ctypes.c_int, _P, _I64, _I64, _P, _I64, _P, ctypes.c_float, _P,
+                                   ctypes.c_int, _P, _P], ctypes.c_int)
 DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 
 EXPORTED = tuple(_SIGS)

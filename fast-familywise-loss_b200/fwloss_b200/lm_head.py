@@ -16,8 +16,10 @@ Backward: the logit gradient of a row has kappa + 1 non-zeros
 (scale / kappa on the support, -scale at the label), so
 dhidden = G W and dweight = G^T hidden become gathers and scatter-adds of
 kappa + 1 rows per sample (fw_sparse_grad_hidden / fw_sparse_grad_weight)
-instead of two dense [B, C] x [C, D] GEMMs.  dweight is accumulated in fp32
-with atomics (the order of the additions is not fixed).
+instead of two dense [B, C] x [C, D] GEMMs.  dweight is written row by row
+(fw_segment_grad_weight): the non-zeros are sorted by column and each touched
+row of dweight sums its contributions in a fixed order, so the result is
+deterministic and only touched rows are written.
 
 Rows where a chunk's own support exceeds K entries (near-constant logits) are
 solved exactly from their full logit rows, and their gradient rows are
@@ -37,6 +39,15 @@ def _logits_chunk(hidden, w_chunk):
     return torch.mm(hidden, w_chunk.t(), out_dtype=torch.float32)
 
 
+_SIDE = {}
+
+
+def _side_stream(dev):
+    if dev not in _SIDE:
+        _SIDE[dev] = torch.cuda.Stream(dev)
+    return _SIDE[dev]
+
+
 def _full_logits(hidden_rows, weight):
     return _logits_chunk(hidden_rows, weight)
 
@@ -52,24 +63,37 @@ class _FWLMHead(torch.autograd.Function):
         summaries = torch.empty((nchunks, B, 4 + K), dtype=torch.int32, device=dev)
         local_idx = torch.empty((nchunks, B, K), dtype=torch.int32, device=dev)
         zy = torch.empty(B, dtype=torch.float32, device=dev)
+        # The GEMM of chunk q+1 (tensor cores) runs while chunk q is being
+        # summarised on a second stream (HBM-bound); a chunk's memory is
+        # released only after its scan (record_stream).
+        main = torch.cuda.current_stream(dev)
+        side = _side_stream(dev)
+        side.wait_stream(main)
         for q in range(nchunks):
             c0, c1 = col_start[q], col_start[q + 1]
             z = _logits_chunk(hidden, weight[c0:c1])
-            fw.shard_scan_into(z, K, summaries[q], local_idx[q])
-            fw.label_logits(z, target, c0, zy)
+            ready = torch.cuda.Event()
+            ready.record(main)
+            with torch.cuda.stream(side):
+                side.wait_event(ready)
+                fw.shard_scan_into(z, K, summaries[q], local_idx[q])
+                fw.label_logits(z, target, c0, zy)
+            z.record_stream(side)
             del z
+        main.wait_stream(side)
         H, kappa, loss_rows, sup_cols, fb_rows, fb_count = fw.chunks_solve(summaries, local_idx, col_start, zy, target)
-        nfb = int(fb_count.item())
+        out = fw.loss_reduce(loss_rows, float(scale))
+        nfb = int(fb_count.item())  # read after the step's work is queued
         rows = g_rows = None
-        if nfb:
+        if nfb:  # rare: rows solved from their full logit rows; their losses were 0 in `out`
             rows = fb_rows[:nfb].long().sort().values
             zf = _full_logits(hidden[rows], weight)
             g_rows, h, l, k = fw.fused_fwd_bwd(zf, target[rows], 1.0, None)
             loss_rows[rows] = l
             H[rows] = h
+            out = out + (l.double().sum() * scale).float()
         ctx.save_for_backward(hidden, weight, target, kappa, sup_cols)
         ctx.rows, ctx.g_rows, ctx.scale = rows, g_rows, float(scale)
-        out = fw.loss_reduce(loss_rows, float(scale))
         return out if hidden.dtype == torch.float32 else out.to(hidden.dtype)
 
     @staticmethod
@@ -81,16 +105,15 @@ class _FWLMHead(torch.autograd.Function):
         if ctx.needs_input_grad[0]:
             dH = fw.sparse_grad_hidden(weight, sup_cols, kappa, target, ctx.scale, go, False)
         if ctx.needs_input_grad[1]:
-            dW32 = torch.zeros(weight.shape, dtype=torch.float32, device=weight.device)
-            fw.sparse_grad_weight(hidden, sup_cols, kappa, target, ctx.scale, go, False, dW32)
+            dW = torch.zeros(weight.shape, dtype=weight.dtype, device=weight.device)
+            keys = torch.sort(fw.weight_grad_keys(sup_cols, kappa, target, weight.shape[0])).values
+            fw.segment_grad_weight(hidden, keys, kappa, ctx.scale, go, False, dW)
         if ctx.rows is not None:  # rows solved from their full logits: dense gradient rows
             gr = ctx.g_rows * (go * ctx.scale)
             if dH is not None:
                 dH[ctx.rows] = (gr @ weight.float()).to(dH.dtype)
-            if ctx.needs_input_grad[1]:
-                dW32 += gr.t() @ hidden[ctx.rows].float()
-        if ctx.needs_input_grad[1]:
-            dW = dW32 if weight.dtype == torch.float32 else dW32.to(weight.dtype)
+            if dW is not None:
+                dW += (gr.t() @ hidden[ctx.rows].float()).to(dW.dtype)
         return dH, dW, None, None, None, None
 
 

@@ -243,6 +243,24 @@ FWB_API int fw_sparse_grad_weight(int dtype, const void* hidden, int64_t B, int6
                                   void* stream);
 
 /*
+ * Deterministic dweight for the LM head, without data-dependent shapes:
+ * fw_weight_grad_keys writes keys[B * (S + 1)], one per non-zero of the logit
+ * gradient, key = (j << 32) | (r << 1) | is_label (unused slots:
+ * 0x7fffffffffffffff); the caller sorts them ascending; then
+ * fw_segment_grad_weight writes, for every column j present,
+ * dweight[j] = sum over its entries, in key order, of g_r / kappa_r * hidden[r]
+ * (support) or -g_r * hidden[r] (label), in the weight's element type.  Rows
+ * of dweight with no entry are not written (caller zeroes them).
+ */
+FWB_API int fw_weight_grad_keys(const int32_t* sup_cols, int S, const int32_t* kappa, const int64_t* y,
+                                int64_t B, int64_t C, int64_t* keys, void* stream);
+
+FWB_API int fw_segment_grad_weight(int dtype, const void* hidden, int64_t B, int64_t D,
+                                   const int64_t* keys, int64_t nkeys, const int32_t* kappa,
+                                   float scale, const float* grad_output, int per_row,
+                                   void* dweight, void* stream);
+
+/*
  * Deterministic (fixed-order, fp64) reduction out[0] = scale * sum_r loss[r].
  * Gives the "mean" (scale 1/B) and "sum" (scale 1) values of the reference
  * (reference_impl.py:28-31, src/cuda/fw_radix_argmax.cu:1411,1493,
