@@ -67,7 +67,7 @@ def parse():
                         "logits = hidden @ weight^T (B=8192, D=4096, C=128256, bf16) with the chunked "
                         "forward and sparse backward, next to the dense path")
     p.add_argument("--shard-k", type=int, default=32, help="class-sharded: support entries per shard summary")
-    p.add_argument("--dtype", default="f32", choices=["f32", "bf16", "f16"],
+    p.add_argument("--dtype", default="f32", choices=["f32", "bf16", "f16", "f64"],
                    help="logits/gradient element type (the metric is defined on f32)")
     return p.parse_args()
 
@@ -76,7 +76,7 @@ def workload_desc(name, B, C, world, esize=4):
     kinds = {"cfg0": "N(0,1)", "cfg1": "N(0,1) +4 at label", "cfg2": "Student-t(3) x2",
              "cfg3": "8 levels + 1% signed zeros", "cfg4": "N(0,1) +8 at a non-label class"}
     return {
-        "workload": f"{name}: FWLoss fwd+bwd, B={B} x C={C}, {dict([(4, 'fp32'), (2, '16-bit')])[esize]} "
+        "workload": f"{name}: FWLoss fwd+bwd, B={B} x C={C}, {dict([(8, 'fp64'), (4, 'fp32'), (2, '16-bit')])[esize]} "
                     f"logits {kinds.get(name, '')}, int64 labels",
         "rows_per_gpu": B, "classes": C, "global_batch": B * world,
         "parallelism": f"row-sharded dp{world}" + (" + scalar NCCL all-reduce" if world > 1 else ""),
@@ -163,9 +163,10 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_baseline(name, B, C, seconds):
+def cpu_baseline(name, B, C, seconds, f64=False):
     """The reference CPU implementation (or the C restatement) on a bounded
-    sample of the workload; returns the cpu_baseline object."""
+    sample of the workload; returns the cpu_baseline object.  f64: float64
+    logits (the reference's float64 branch; there is no float64 port)."""
     import torch
     from fwloss_b200 import workloads
 
@@ -173,6 +174,8 @@ def cpu_baseline(name, B, C, seconds):
     torch.set_num_threads(threads)
     rows = min(B, 1024)
     z, y = workloads.make(name, rows=rows)
+    if f64:
+        z = z.double()
     try:
         from oracle import ref_cpu
 
@@ -273,7 +276,7 @@ def run_ours(a):
     # inputs: rank 0 gets the configuration itself, other ranks the same recipe
     # with their own seed (weak scaling: every rank owns B distinct rows)
     z_cpu, y_cpu = workloads.make_rank(a.config, rank)
-    tdt = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[a.dtype]
+    tdt = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16, "f64": torch.float64}[a.dtype]
     esize = torch.tensor([], dtype=tdt).element_size()
     z_cpu = z_cpu.to(tdt)
     # inputs larger than L2 (126 MB): small configurations rotate over enough
@@ -377,7 +380,7 @@ def run_ours(a):
     kd1.record(stream)
     torch.cuda.synchronize(dev)
     k_ms = kd0.elapsed_time(kd1) / a.steps
-    alg_bytes = B * (2 * esize * C + 12)
+    alg_bytes = B * (2 * esize * C + (16 if esize == 8 else 12))  # + label, loss
     achieved = alg_bytes / (k_ms / 1e3) / 1e9
     peak, peak_kind = measured_peak()
 
@@ -425,7 +428,7 @@ def run_ours(a):
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         try:
-            cpu = cpu_baseline(a.config, B, C, a.cpu_seconds)
+            cpu = cpu_baseline(a.config, B, C, a.cpu_seconds, f64=a.dtype == "f64")
         except Exception as ex:  # report, do not fail the GPU measurement
             cpu = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "unavailable",
                    "sample": f"failed: {ex!r}"[:200]}
@@ -439,9 +442,10 @@ def run_ours(a):
             "config": dict(workload_desc(a.config, B, C, world, esize),
                            launch="CUDA-graph replay of each step" if use_graph else "eager"),
             "hbm_gbs": alg_bytes * a.steps / (ms / 1e3) / 1e9,
-            "roofline": {"bound": "hbm", "kernel": "fw_stream_rows_kernel" if C > 2048 else "fw_warp_rows_kernel",
+            "roofline": {"bound": "hbm", "kernel": ("fw_f64_rows_kernel" if esize == 8 else
+                                                    "fw_stream_rows_kernel" if C > 2048 else "fw_warp_rows_kernel"),
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_kind": peak_kind, "traffic": profile_traffic(a.config),
+                         "peak_kind": peak_kind, "traffic": profile_traffic(a.config if a.dtype == "f32" else f"{a.config}_{a.dtype}"),
                          "alg_bytes_per_launch": alg_bytes, "kernel_ms": k_ms},
             "cpu_baseline": cpu,
             "e2e": e2e,

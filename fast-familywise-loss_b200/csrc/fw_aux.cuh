@@ -141,11 +141,13 @@ __global__ void __launch_bounds__(kAuxThreads)
 }
 
 // out[0] = scale * sum(loss[0..B)), fp64 accumulation in a fixed order (one
-// CTA; thread t sums t, t + 1024, ...; then a fixed tree).
+// CTA; thread t sums t, t + 1024, ...; then a fixed tree).  T: fp32 or fp64
+// losses and result.
 constexpr int kReduceThreads = 1024;
+template <class T>
 __global__ void __launch_bounds__(kReduceThreads)
-    fw_loss_reduce_kernel(const float* __restrict__ loss, int64_t B,
-                          double scale, float* __restrict__ out) {
+    fw_loss_reduce_kernel(const T* __restrict__ loss, int64_t B,
+                          double scale, T* __restrict__ out) {
   __shared__ double part[kReduceThreads / 32];
   double s = 0.0;
   for (int64_t i = threadIdx.x; i < B; i += kReduceThreads) s += (double)loss[i];
@@ -155,7 +157,7 @@ __global__ void __launch_bounds__(kReduceThreads)
   if (threadIdx.x < 32) {
     double t = part[threadIdx.x];
     t = warp_sum(t);
-    if (threadIdx.x == 0) out[0] = (float)(t * scale);
+    if (threadIdx.x == 0) out[0] = (T)(t * scale);
   }
 }
 

@@ -18,6 +18,7 @@
 #include "../../include/fwloss_b200.h"
 #include "fw_aux.cuh"
 #include "fw_device.cuh"
+#include "fw_f64.cuh"
 #include "fw_lmhead.cuh"
 #include "fw_shard.cuh"
 #include "fw_stream_tier.cuh"
@@ -162,6 +163,23 @@ RowArgs base_args(const void* z, const int64_t* y, int64_t B, int64_t C, int64_t
   a.kappa = kappa;
   a.status = status;
   return a;
+}
+
+// fp64 rows: a warp per row up to kF64WarpRowMaxC columns, a CTA per row
+// beyond; grid capped at the resident CTAs (rows are looped over).
+template <int TW, bool VEC>
+cudaError_t launch_f64(const F64Args& a, cudaStream_t st) {
+  auto k = fw_f64_rows_kernel<TW, VEC>;
+  static int occ = 0;
+  if (occ == 0) {
+    int r = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, k, kF64Threads, 0) != cudaSuccess || r < 1) r = 1;
+    occ = r;
+  }
+  constexpr int64_t rows_per_block = kF64Warps / TW;
+  const int64_t need = (a.B + rows_per_block - 1) / rows_per_block;
+  const int64_t cap = (int64_t)sm_count() * occ;
+  return launch(k, dim3((unsigned)(need < cap ? need : cap)), dim3(kF64Threads), 1, st, a);
 }
 
 int aux_grid(int64_t rows, int per_block) {
@@ -464,8 +482,42 @@ int fw_segment_grad_weight(int dtype, const void* hidden, int64_t B, int64_t D, 
 int fw_loss_reduce(const float* loss, int64_t B, double scale, float* out, void* stream) {
   if (B < 0) return FWB_E_SHAPE;
   if (!out || (B > 0 && !loss)) return FWB_E_POINTER;
-  return launch_status(launch(fw_loss_reduce_kernel, dim3(1), dim3(kReduceThreads), 1,
+  return launch_status(launch(fw_loss_reduce_kernel<float>, dim3(1), dim3(kReduceThreads), 1,
                               static_cast<cudaStream_t>(stream), loss, B, scale, out));
+}
+
+int fw_loss_reduce_f64(const double* loss, int64_t B, double scale, double* out, void* stream) {
+  if (B < 0) return FWB_E_SHAPE;
+  if (!out || (B > 0 && !loss)) return FWB_E_POINTER;
+  return launch_status(launch(fw_loss_reduce_kernel<double>, dim3(1), dim3(kReduceThreads), 1,
+                              static_cast<cudaStream_t>(stream), loss, B, scale, out));
+}
+
+int fw_fused_fwd_bwd_f64(const double* z, const int64_t* y, int64_t B, int64_t C, int64_t ld,
+                         double grad_scale, double* grad, double* H, double* loss, int32_t* kappa,
+                         int32_t* status, void* stream) {
+  if (int rc = check_shape(B, C, ld)) return rc;
+  if (B == 0) return FWB_OK;
+  if (!z || !y || !grad) return FWB_E_POINTER;
+  const F64Args a = {z, y, B, C, ld, grad_scale, grad, H, loss, kappa, status};
+  const bool vec = aligned16(z) && aligned16(grad) && (ld % 2 == 0);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (C <= kF64WarpRowMaxC)
+    e = vec ? launch_f64<1, true>(a, st) : launch_f64<1, false>(a, st);
+  else
+    e = vec ? launch_f64<kF64Warps, true>(a, st) : launch_f64<kF64Warps, false>(a, st);
+  return launch_status(e);
+}
+
+int fw_scale_grad_f64(double* grad, const double* grad_output, int per_row, double assumed_scale,
+                      int64_t B, int64_t C, int64_t ld, void* stream) {
+  if (int rc = check_shape(B, C, ld)) return rc;
+  if (B == 0) return FWB_OK;
+  if (!grad || !grad_output) return FWB_E_POINTER;
+  return launch_status(launch(fw_scale_grad_f64_kernel, dim3(aux_grid(B, 1)), dim3(256), 1,
+                              static_cast<cudaStream_t>(stream), grad, grad_output, per_row,
+                              assumed_scale, B, C, ld));
 }
 
 }  // extern "C"

@@ -37,8 +37,8 @@ void check_logits(const torch::Tensor& logits, bool any_float = false) {
   TORCH_CHECK(logits.dim() == 2, "logits must have shape [N, K]");
   if (any_float) {
     TORCH_CHECK(logits.scalar_type() == torch::kFloat32 || logits.scalar_type() == torch::kBFloat16 ||
-                    logits.scalar_type() == torch::kHalf,
-                "logits must be float32, bfloat16 or float16");
+                    logits.scalar_type() == torch::kHalf || logits.scalar_type() == torch::kFloat64,
+                "logits must be float32, bfloat16, float16 or float64");
   } else {
     TORCH_CHECK(logits.scalar_type() == torch::kFloat32, "logits must be float32");
   }
@@ -189,8 +189,9 @@ torch::Tensor fw_backward(torch::Tensor logits, torch::Tensor targets, torch::Te
 }
 
 // Fused forward + backward (new): (grad, H, losses, kappa), grad scaled by
-// grad_scale and of the logits' dtype (float32, bfloat16 or float16), H and
-// losses float32; `status` is an optional int32 [1] device word.
+// grad_scale and of the logits' dtype (float32, bfloat16, float16 or
+// float64); H and losses float32 (float64 for float64 logits); `status` is an
+// optional int32 [1] device word.
 std::vector<torch::Tensor> fused_fwd_bwd(torch::Tensor logits, torch::Tensor targets,
                                          double grad_scale, c10::optional<torch::Tensor> status) {
   check_logits(logits, true);
@@ -202,14 +203,23 @@ std::vector<torch::Tensor> fused_fwd_bwd(torch::Tensor logits, torch::Tensor tar
   auto y = targets.contiguous();
   auto grad = (ld == K) ? torch::empty({N, K}, logits.options())
                         : torch::empty_strided({N, K}, {ld, 1}, logits.options());
-  auto H = torch::empty({N}, logits.options().dtype(torch::kFloat32));
-  auto losses = torch::empty({N}, logits.options().dtype(torch::kFloat32));
+  const bool f64 = z.scalar_type() == torch::kFloat64;
+  const auto out_t = f64 ? torch::kFloat64 : torch::kFloat32;
+  auto H = torch::empty({N}, logits.options().dtype(out_t));
+  auto losses = torch::empty({N}, logits.options().dtype(out_t));
   auto kappa = torch::empty({N}, i32(logits));
   int32_t* st = nullptr;
   if (status.has_value()) {
     TORCH_CHECK(status->is_cuda() && status->scalar_type() == torch::kInt32 && status->numel() >= 1,
                 "status must be an int32 CUDA tensor");
     st = status->data_ptr<int32_t>();
+  }
+  if (f64) {
+    check_rc(fw_fused_fwd_bwd_f64(z.data_ptr<double>(), y.data_ptr<int64_t>(), N, K, ld, grad_scale,
+                                  grad.data_ptr<double>(), H.data_ptr<double>(), losses.data_ptr<double>(),
+                                  kappa.data_ptr<int32_t>(), st, cur_stream()),
+             "fw_fused_fwd_bwd_f64");
+    return {grad, H, losses, kappa};
   }
   check_rc(fw_fused_fwd_bwd_typed(dtype_code(z), z.data_ptr(), y.data_ptr<int64_t>(), N, K, ld,
                                   (float)grad_scale, grad.data_ptr(), H.data_ptr<float>(),
@@ -222,24 +232,39 @@ std::vector<torch::Tensor> fused_fwd_bwd(torch::Tensor logits, torch::Tensor tar
 void scale_grad(torch::Tensor grad, torch::Tensor grad_output, bool per_row, double assumed_scale) {
   TORCH_CHECK(grad.is_cuda() && grad.dim() == 2 && grad.stride(1) == 1 &&
                   (grad.scalar_type() == torch::kFloat32 || grad.scalar_type() == torch::kBFloat16 ||
-                   grad.scalar_type() == torch::kHalf),
-              "grad must be a row-major float32/bfloat16/float16 CUDA matrix");
+                   grad.scalar_type() == torch::kHalf || grad.scalar_type() == torch::kFloat64),
+              "grad must be a row-major float32/bfloat16/float16/float64 CUDA matrix");
   const c10::cuda::CUDAGuard guard(grad.device());
+  const int64_t ld = grad.size(0) > 1 ? grad.stride(0) : grad.size(1);
+  if (grad.scalar_type() == torch::kFloat64) {
+    auto go = grad_output.to(grad.device(), torch::kFloat64).contiguous();
+    TORCH_CHECK(go.numel() >= (per_row ? grad.size(0) : 1), "grad_output too small");
+    check_rc(fw_scale_grad_f64(grad.data_ptr<double>(), go.data_ptr<double>(), per_row ? 1 : 0,
+                               assumed_scale, grad.size(0), grad.size(1), ld, cur_stream()),
+             "fw_scale_grad_f64");
+    return;
+  }
   auto go = grad_output.to(grad.device(), torch::kFloat32).contiguous();
   TORCH_CHECK(go.numel() >= (per_row ? grad.size(0) : 1), "grad_output too small");
-  const int64_t ld = grad.size(0) > 1 ? grad.stride(0) : grad.size(1);
   check_rc(fw_scale_grad_typed(dtype_code(grad), grad.data_ptr(), go.data_ptr<float>(), per_row ? 1 : 0,
                                (float)assumed_scale, grad.size(0), grad.size(1), ld, cur_stream()),
            "fw_scale_grad");
 }
 
-// scale * sum(losses), fixed-order fp64 reduction; 0-d float32.
+// scale * sum(losses), fixed-order fp64 reduction; 0-d, of the losses' dtype
+// (float32 or float64).
 torch::Tensor loss_reduce(torch::Tensor losses, double scale) {
-  TORCH_CHECK(losses.is_cuda() && losses.scalar_type() == torch::kFloat32 && losses.dim() == 1,
-              "losses must be a float32 CUDA vector");
+  TORCH_CHECK(losses.is_cuda() && losses.dim() == 1 &&
+                  (losses.scalar_type() == torch::kFloat32 || losses.scalar_type() == torch::kFloat64),
+              "losses must be a float32 or float64 CUDA vector");
   const c10::cuda::CUDAGuard guard(losses.device());
   auto l = losses.contiguous();
   auto out = torch::empty({}, l.options());
+  if (l.scalar_type() == torch::kFloat64) {
+    check_rc(fw_loss_reduce_f64(l.data_ptr<double>(), l.size(0), scale, out.data_ptr<double>(), cur_stream()),
+             "fw_loss_reduce_f64");
+    return out;
+  }
   check_rc(fw_loss_reduce(l.data_ptr<float>(), l.size(0), scale, out.data_ptr<float>(), cur_stream()),
            "fw_loss_reduce");
   return out;

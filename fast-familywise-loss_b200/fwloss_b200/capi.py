@@ -47,7 +47,12 @@ _SIGS["fw_sparse_grad_weight"] = ([ctypes.c_int, _P, _I64, _I64, _P, ctypes.c_in
 _SIGS["fw_weight_grad_keys"] = ([_P, ctypes.c_int, _P, _P, _I64, _I64, _P, _P], ctypes.c_int)
 _SIGS["fw_segment_grad_weight"] = ([ctypes.c_int, _P, _I64, _I64, _P, _I64, _P, ctypes.c_float, _P,
                                    ctypes.c_int, _P, _P], ctypes.c_int)
+_SIGS["fw_fused_fwd_bwd_f64"] = ([_P, _P, _I64, _I64, _I64, ctypes.c_double, _P, _P, _P, _P, _P, _P],
+                                 ctypes.c_int)
+_SIGS["fw_scale_grad_f64"] = ([_P, _P, ctypes.c_int, ctypes.c_double, _I64, _I64, _I64, _P], ctypes.c_int)
+_SIGS["fw_loss_reduce_f64"] = ([_P, _I64, ctypes.c_double, _P, _P], ctypes.c_int)
 DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+_ANY_FLOAT = (torch.float32, torch.bfloat16, torch.float16, torch.float64)
 
 EXPORTED = tuple(_SIGS)
 
@@ -91,9 +96,9 @@ def _check(rc, what):
 
 
 def _rows(z, any_float=False):
-    if z.dim() != 2 or not z.is_cuda or z.dtype not in (DTYPE_CODES if any_float else (torch.float32,)):
+    if z.dim() != 2 or not z.is_cuda or z.dtype not in (_ANY_FLOAT if any_float else (torch.float32,)):
         raise FWError("logits must be a 2-D float32 CUDA tensor" +
-                      (" (or bfloat16 / float16)" if any_float else ""))
+                      (" (or bfloat16 / float16 / float64)" if any_float else ""))
     if z.stride(1) != 1 or (z.size(0) > 1 and z.stride(0) < z.size(1)):
         z = z.contiguous()
     ld = z.stride(0) if z.size(0) > 1 else z.size(1)
@@ -103,17 +108,22 @@ def _rows(z, any_float=False):
 def fused_fwd_bwd(z, y, grad_scale, grad=None, status=None):
     """(grad, H, loss, kappa) from the fused kernel; grad has z's row stride
     and dtype (float32 logits use fw_fused_fwd_bwd, 16-bit logits
-    fw_fused_fwd_bwd_typed)."""
+    fw_fused_fwd_bwd_typed, float64 logits fw_fused_fwd_bwd_f64 with fp64 H
+    and loss)."""
     z, ld = _rows(z, any_float=True)
     B, C = z.shape
     if grad is None:
         grad = torch.empty_strided((B, C), (ld, 1), dtype=z.dtype, device=z.device)
-    H = torch.empty(B, dtype=torch.float32, device=z.device)
-    loss = torch.empty(B, dtype=torch.float32, device=z.device)
+    f64 = z.dtype == torch.float64
+    H = torch.empty(B, dtype=torch.float64 if f64 else torch.float32, device=z.device)
+    loss = torch.empty(B, dtype=H.dtype, device=z.device)
     kappa = torch.empty(B, dtype=torch.int32, device=z.device)
     lib = load()
     with torch.cuda.device(z.device):
-        if z.dtype == torch.float32:
+        if f64:
+            rc = lib.fw_fused_fwd_bwd_f64(_ptr(z), _ptr(y), B, C, ld, float(grad_scale), _ptr(grad),
+                                          _ptr(H), _ptr(loss), _ptr(kappa), _ptr(status), _stream(z))
+        elif z.dtype == torch.float32:
             rc = lib.fw_fused_fwd_bwd(_ptr(z), _ptr(y), B, C, ld, float(grad_scale), _ptr(grad),
                                       _ptr(H), _ptr(loss), _ptr(kappa), _ptr(status), _stream(z))
         else:
@@ -177,6 +187,12 @@ def backward_candidates(cv, ci, cc, H, kappa, y, grad_scale, status=None):
 def scale_grad(grad, grad_output, per_row, assumed_scale):
     B, C = grad.shape
     ld = grad.stride(0) if B > 1 else C
+    if grad.dtype == torch.float64:
+        go = grad_output.to(torch.float64)
+        with torch.cuda.device(grad.device):
+            _check(load().fw_scale_grad_f64(_ptr(grad), _ptr(go), int(bool(per_row)), float(assumed_scale),
+                                            B, C, ld, _stream(grad)), "fw_scale_grad_f64")
+        return grad
     go = grad_output.to(torch.float32)
     with torch.cuda.device(grad.device):
         _check(load().fw_scale_grad_typed(DTYPE_CODES[grad.dtype], _ptr(grad), _ptr(go), int(bool(per_row)),
@@ -185,10 +201,11 @@ def scale_grad(grad, grad_output, per_row, assumed_scale):
 
 
 def loss_reduce(loss, scale):
-    out = torch.empty((), dtype=torch.float32, device=loss.device)
+    """scale * sum(loss) for float32 or float64 losses (result of the same dtype)."""
+    out = torch.empty((), dtype=loss.dtype, device=loss.device)
+    fn = load().fw_loss_reduce_f64 if loss.dtype == torch.float64 else load().fw_loss_reduce
     with torch.cuda.device(loss.device):
-        _check(load().fw_loss_reduce(_ptr(loss), loss.numel(), float(scale), _ptr(out),
-                                     _stream(loss)), "fw_loss_reduce")
+        _check(fn(_ptr(loss), loss.numel(), float(scale), _ptr(out), _stream(loss)), "fw_loss_reduce")
     return out
 
 

@@ -23,8 +23,8 @@ _REDUCTIONS = ("mean", "sum", "none")
 def _check_inputs(logits, target):
     if not (isinstance(logits, torch.Tensor) and logits.is_cuda):
         raise TypeError("familywise_loss: logits must be a CUDA tensor (this build has no CPU path)")
-    if logits.dim() != 2 or logits.dtype not in (torch.float32, torch.bfloat16, torch.float16):
-        raise TypeError("familywise_loss: logits must be a 2-D float32, bfloat16 or float16 tensor [N, K]")
+    if logits.dim() != 2 or logits.dtype not in (torch.float32, torch.bfloat16, torch.float16, torch.float64):
+        raise TypeError("familywise_loss: logits must be a 2-D float32, bfloat16, float16 or float64 tensor [N, K]")
     if target.dim() != 1 or target.shape[0] != logits.shape[0]:
         raise ValueError("familywise_loss: target must have shape [N]")
     if target.dtype != torch.int64:
@@ -84,7 +84,8 @@ class _MeanOfRows(torch.autograd.Function):
     @staticmethod
     def forward(ctx, losses):
         ctx.n = losses.shape[0]
-        out = ext().loss_reduce(losses.float(), 1.0 / ctx.n if ctx.n else float("nan"))
+        wide = losses if losses.dtype == torch.float64 else losses.float()
+        out = ext().loss_reduce(wide, 1.0 / ctx.n if ctx.n else float("nan"))
         return out if losses.dtype == torch.float32 else out.to(losses.dtype)
 
     @staticmethod
@@ -97,7 +98,8 @@ def familywise_loss(logits, target, reduction="mean", status=None):
 
     reduction "mean" / "sum" return a 0-d tensor, "none" the per-row losses.
     bfloat16 / float16 logits are accepted (fp32 arithmetic; gradient and loss
-    in the logits' dtype).
+    in the logits' dtype), and float64 logits (fp64 arithmetic, gradient and
+    loss; the reference CPU kernel's float64 path, src/cpu/fw_cpu.cpp:698-704).
     `status`, if given, is an int32 CUDA tensor whose first word receives the
     bit-or of FWB_STATUS_* flags (label out of range, non-finite row).
     """
@@ -112,7 +114,7 @@ def familywise_loss(logits, target, reduction="mean", status=None):
 
 
 def fw_rows(logits, target, assumed_scale=1.0, status=None):
-    """(losses [N] differentiable, H [N] fp32, kappa [N] int32)."""
+    """(losses [N] differentiable, H [N] fp32 (fp64 for float64 logits), kappa [N] int32)."""
     _check_inputs(logits, target)
     return _FWRows.apply(logits, target, float(assumed_scale), status)
 

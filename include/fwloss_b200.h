@@ -269,6 +269,30 @@ FWB_API int fw_segment_grad_weight(int dtype, const void* hidden, int64_t B, int
 FWB_API int fw_loss_reduce(const float* loss, int64_t B, double scale, float* out,
                    void* stream);
 
+/*
+ * float64 logits: fw_fused_fwd_bwd with fp64 logits, gradient, H and loss
+ * (grad: [B, ld] fp64, same row stride as z).  Replaces the float64 branch of
+ * the reference CPU kernel (src/cpu/fw_cpu.cpp:698-704, fw_row<double> at
+ * :419-470); the reference CUDA kernels are fp32-only.  Support:
+ * {x > t0 and fl(x - M) > tau} with t0 = M - 1 rounded down, which is the
+ * exact support whenever the row max M >= 2 and otherwise agrees with it up
+ * to fp64 rounding; H = fl(M + tau).
+ */
+FWB_API int fw_fused_fwd_bwd_f64(const double* z, const int64_t* y, int64_t B, int64_t C,
+                                 int64_t ld, double grad_scale, double* grad, double* H,
+                                 double* loss, int32_t* kappa, int32_t* status, void* stream);
+
+/* fw_scale_grad for an fp64 gradient with fp64 grad_output (FWFunction::backward,
+ * src/cpu/fw_cpu.cpp:734-740, for float64 logits). */
+FWB_API int fw_scale_grad_f64(double* grad, const double* grad_output, int per_row,
+                              double assumed_scale, int64_t B, int64_t C, int64_t ld,
+                              void* stream);
+
+/* fw_loss_reduce for fp64 losses and an fp64 result (the float64 total of
+ * src/cpu/fw_cpu.cpp:729-732). */
+FWB_API int fw_loss_reduce_f64(const double* loss, int64_t B, double scale, double* out,
+                               void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -152,3 +152,68 @@ def solve(z, y, scale=None):
         "H": threshold_f32(tau, M), "mask": mask,
         "grad": dense_grad(mask, kappa, y, scale),
     }
+
+
+def round_down_minus1_f64(M):
+    """t0 of the float64 kernels: the largest float64 <= M - 1, elementwise
+    (NaN and +-inf pass).  M - 1 is formed in float64 and corrected by its
+    exact rounding error (two-sum)."""
+    M = np.asarray(M, dtype=np.float64)
+    with np.errstate(invalid="ignore"):
+        s = M - 1.0
+        bb = s - M
+        err = (M - (s - bb)) + (-1.0 - bb)   # s + err == M - 1 exactly
+        return np.where(np.isfinite(s) & (err < 0), np.nextafter(s, -np.inf), s)
+
+
+def solve_f64(z, y, scale=None):
+    """Everything fw_fused_fwd_bwd_f64 produces for float64 logits z [B, C]:
+    dict with tau, M, kappa, H = M + tau, loss, mask and the dense gradient
+    (all float64).
+
+    Restates reference_impl.FWLoss.forward (reference_impl.py:11-26) on
+    float64 rows, on the candidates above t0 = M - 1 rounded down and in the
+    shifted domain d = fl(z - M) (as the reference CPU kernel's float64 path
+    falls back to, src/cpu/fw_cpu.cpp:462-468): sort d descending,
+    h_k = (S_k - 1)/k, tau = h at the first argmax, support
+    {z > t0 and d > tau}, loss = (1 + (M - z_y)) + tau.  Rows with a
+    non-finite maximum follow nonfinite_policy(); rows whose label is outside
+    [0, C) get a NaN loss and no label term in the gradient.
+    """
+    z = np.asarray(z, dtype=np.float64)
+    y = np.asarray(y, dtype=np.int64)
+    B, C = z.shape
+    if scale is None:
+        scale = 1.0 / B if B else 1.0
+    ok_y = (y >= 0) & (y < C)
+    yc = np.where(ok_y, y, 0)
+    M = np.max(z, axis=1) if C else np.zeros(B)
+    tau = np.zeros(B)
+    kappa = np.ones(B, dtype=np.int64)
+    loss = np.empty(B)
+    mask = np.zeros((B, C), dtype=bool)
+    finite = np.isfinite(M) & ~np.isnan(z).any(axis=1)
+    t0 = round_down_minus1_f64(M)
+    for r in np.nonzero(finite)[0]:
+        d = z[r] - M[r]
+        cand = z[r] > t0[r]
+        ds = -np.sort(-d[cand])
+        S = np.cumsum(ds)
+        hk = (S - 1.0) / np.arange(1, ds.size + 1, dtype=np.float64)
+        k = int(np.argmax(hk))            # first maximal index
+        tau[r] = hk[k]
+        kappa[r] = k + 1
+        mask[r] = cand & (d > tau[r])
+        loss[r] = (1.0 + (M[r] - z[r, yc[r]])) + tau[r]
+    for r in np.nonzero(~finite)[0]:
+        j, Mr = nonfinite_policy(z[r])
+        M[r] = Mr
+        mask[r, j] = True
+        loss[r] = 1.0 - z[r, yc[r]] + Mr
+    loss = np.where(ok_y, loss, np.nan)
+    inv = scale / kappa.astype(np.float64)
+    grad = mask.astype(np.float64) * inv[:, None]
+    rows = np.nonzero(ok_y)[0]
+    grad[rows, y[rows]] -= scale
+    H = np.where(finite, M + tau, M)
+    return {"tau": tau, "M": M, "kappa": kappa, "loss": loss, "H": H, "mask": mask, "grad": grad}

@@ -70,6 +70,19 @@ def ref_loss_grad(z, y, scale):
     return L.numpy(), G.numpy(), K.numpy()
 
 
+def ref_loss_grad64(z, y, scale):
+    """(loss [B] f64, grad [B, C] f64 scaled, kappa [B] i64) from the
+    reference CPU code on float64 logits (fw_loss_grad, its float64 branch,
+    src/cpu/fw_cpu.cpp:698-704)."""
+    import torch
+
+    m = ref_module()
+    Z = torch.as_tensor(np.ascontiguousarray(z, dtype=np.float64))
+    Y = torch.as_tensor(np.ascontiguousarray(y, dtype=np.int64))
+    L, G, K = m.fw_loss_grad(Z, Y, float(scale), 2 ** 62, 100_000, True)
+    return L.numpy(), G.numpy(), K.numpy()
+
+
 def c_oracle():
     global _oracle
     if _oracle is None:

@@ -186,3 +186,75 @@ def nonfinite_cases():
         return z, _labels(r, 5, 40)
 
     return [("nonfinite_C3000", g_nan), ("nonfinite_C40", g_small)]
+
+
+# --------------------------------------------------------------- float64 rows
+def as_f64(gen):
+    """A float32 case's values, as float64 rows."""
+    def g():
+        z, y = gen()
+        return z.astype(np.float64), y
+    return g
+
+
+def gauss64(B, C, sigma=1.0, seed=0, offset=0.0):
+    """float64 values with bits below float32 resolution."""
+    def g():
+        r = _rng(seed)
+        z = offset + r.standard_normal((B, C)) * sigma
+        return z, _labels(r, B, C)
+    return g
+
+
+def fine64(B, C, step, seed=0):
+    """Rows 0.5 + j * step in random order: neighbours closer than a float32
+    ulp, so the support is decided by float64 bits only."""
+    def g():
+        r = _rng(seed)
+        z = 0.5 + np.stack([r.permutation(C) for _ in range(B)]).astype(np.float64) * step
+        return z, _labels(r, B, C)
+    return g
+
+
+def magnitude64(B, C, scale, seed=0):
+    def g():
+        r = _rng(seed)
+        z = r.standard_normal((B, C)) * scale
+        z[0, : max(1, C // 3)] = z[0].max()
+        return z, _labels(r, B, C)
+    return g
+
+
+def f64_cases():
+    """(name, generator) for float64 logits; generators return float64 z."""
+    cases = []
+    for C in [1, 2, 3, 7, 31, 32, 33, 100, 128, 511, 1023, 1024, 1025, 2048, 5001, 32000]:
+        cases.append((f"f64_gauss_C{C}", gauss64(6, C, 1.0, seed=100 + C)))
+    cases += [
+        ("f64_gauss_off1e6_C700", gauss64(6, 700, 0.5, seed=201, offset=1e6)),
+        ("f64_gauss_off1e6_C9000", gauss64(4, 9000, 0.5, seed=202, offset=1e6)),
+        ("f64_fine_C200", fine64(6, 200, 1e-12, seed=203)),          # dense, one warp per row
+        ("f64_fine_C3000", fine64(4, 3000, 1e-4, seed=204)),          # dense, one CTA per row
+        ("f64_fine_C2000_s1e-3", fine64(4, 2000, 1e-3, seed=205)),   # support ~ sqrt(2000)
+        ("f64_dense_s1e-3_C1000", gauss64(6, 1000, 1e-3, seed=206)),
+        ("f64_dense_s1e-3_C40000", gauss64(2, 40000, 1e-3, seed=207)),
+        ("f64_ties_C128", as_f64(levels(32, 128, [-3.5, -2.5, -1.5, -0.5, 0.5, 1.5, 2.5, 3.5], seed=208))),
+        ("f64_ties_C5000", as_f64(levels(8, 5000, [-1.0, 0.0, 1.0, 2.0], seed=209))),
+        ("f64_const_C5", as_f64(constant(4, 5, 2.0))),
+        ("f64_const_C3000", as_f64(constant(3, 3000, 1.0))),
+        ("f64_sorted_C1000", as_f64(sorted_rows(8, 1000, seed=210))),
+        ("f64_twolevel_C20000", as_f64(two_level(4, 20000, seed=211))),
+        ("f64_outlier_C1000", as_f64(outliers(8, 1000, seed=212))),
+        ("f64_zeros_C100", as_f64(signed_zeros(16, 100, seed=213))),
+        ("f64_neginf_C500", as_f64(neg_inf(8, 500, seed=214))),
+        ("f64_neginf_C12000", as_f64(neg_inf(4, 12000, seed=215))),
+        ("f64_exact_ties", as_f64(exact_ties(seed=216))),
+        ("f64_mag1e200_C64", magnitude64(6, 64, 1e200, seed=217)),
+        ("f64_mag1e200_C5000", magnitude64(4, 5000, 1e200, seed=218)),
+        ("f64_mag1e-200_C300", magnitude64(6, 300, 1e-200, seed=219)),
+    ]
+    return cases
+
+
+def f64_nonfinite_cases():
+    return [(name.replace("nonfinite", "f64_nonfinite"), as_f64(g)) for name, g in nonfinite_cases()]

@@ -12,6 +12,11 @@ see tests/cases.py and fwloss_b200.workloads):
                          extension (src/cpu/fw_cpu.cpp, fw_loss_grad) return:
                          kappa, H, per-row loss and the gradient (sparse:
                          row, col, value) for reduction "mean".
+  reference_outputs_f64.npz
+                         the same for the float64 cases (cases.f64_cases):
+                         reference_impl.FWLoss on float64 tensors and the
+                         CPU extension's float64 branch (fw_cpu.cpp:698-704);
+                         gradients in float64.
   kat_kbar.json          the known answers the reference ships: the `kbar`
                          (mean kappa over 32 rows) of every (distribution,
                          sigma, K) in benchmarks/cpu_benchmarks/results/*.json,
@@ -68,6 +73,27 @@ def reference_outputs(z, y):
     return out
 
 
+def reference_outputs_f64(z, y):
+    B, C = z.shape
+    zt = torch.from_numpy(z).clone().requires_grad_(True)
+    yt = torch.from_numpy(y)
+    H, losses, mean, kappas = reference_impl.FWLoss(C, reduction="mean")(zt, yt)
+    mean.backward()
+    L, G, K = ref_cpu.ref_loss_grad64(z, y, 1.0 / B)
+    out = {
+        "kappa_ref64": kappas.numpy().astype(np.int64),
+        "H_ref64": H.detach().numpy().astype(np.float64),
+        "loss_ref64": losses.detach().numpy().astype(np.float64),
+        "kappa_cpu64": K.astype(np.int64),
+        "loss_cpu64": L.astype(np.float64),
+    }
+    for tag, g in (("grad_ref64", zt.grad.numpy()), ("grad_cpu64", G)):
+        r, c = np.nonzero(g)
+        out[tag + "_r"], out[tag + "_c"] = r.astype(np.int32), c.astype(np.int32)
+        out[tag + "_v"] = g[r, c].astype(np.float64)
+    return out
+
+
 def all_cases():
     for name, gen in cases.parity_cases(full=False):
         yield name, gen
@@ -102,6 +128,13 @@ def main():
             store[f"{name}/{k}"] = v
         print(name, z.shape, flush=True)
     np.savez_compressed(os.path.join(HERE, "reference_outputs.npz"), **store)
+    store64 = {}
+    for name, gen in cases.f64_cases():
+        z, y = gen()
+        for k, v in reference_outputs_f64(z, y).items():
+            store64[f"{name}/{k}"] = v
+        print(name, z.shape, flush=True)
+    np.savez_compressed(os.path.join(HERE, "reference_outputs_f64.npz"), **store64)
     with open(os.path.join(HERE, "kat_kbar.json"), "w") as f:
         json.dump(kat(), f, indent=1)
 

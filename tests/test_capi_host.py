@@ -60,6 +60,12 @@ def test_argument_checks_without_device():
     assert lib.fw_loss_reduce(dummy, 4, 1.0, P, P) == 2
     # an empty batch is a valid no-op (no launch)
     assert lib.fw_fused_fwd_bwd(P, P, 0, 10, 10, 1.0, P, P, P, P, P, P) == 0
+    # float64 entry points: same checks
+    assert lib.fw_fused_fwd_bwd_f64(dummy, dummy, 4, 10, 9, 1.0, dummy, P, P, P, P, P) == 1
+    assert lib.fw_fused_fwd_bwd_f64(dummy, dummy, 4, 10, 10, 1.0, P, P, P, P, P, P) == 2
+    assert lib.fw_fused_fwd_bwd_f64(P, P, 0, 10, 10, 1.0, P, P, P, P, P, P) == 0
+    assert lib.fw_scale_grad_f64(dummy, P, 0, 1.0, 4, 10, 10, P) == 2
+    assert lib.fw_loss_reduce_f64(dummy, 4, 1.0, P, P) == 2
 
 
 def test_dropin_module_surface():

@@ -95,3 +95,51 @@ def test_oracle_reproduces_reference_kbar(fname):
         assert float(np.mean(kap)) == kbar, (fname, s, K)
         n += 1
     assert n == len(entry["Ks"]) * len(entry["stds"])
+
+
+# ------------------------------------------------------------ float64 logits
+GOLDEN64 = np.load(__import__("os").path.join(__import__("os").path.dirname(__file__), "golden",
+                                              "reference_outputs_f64.npz"))
+NAMES64 = sorted({k.split("/")[0] for k in GOLDEN64.files})
+# reference_impl.py:7-8 builds kappa_inv = 1 / arange(1, K + 1) in the default
+# float32 dtype, so on float64 logits its h_k carry float32-rounded 1/k
+# factors (H off by ~1e-8); on these rows that moves its argmax (offset 1e6,
+# exact ties, and 1e200 magnitudes where S_k - 1 == S_k unshifted).
+REF64_ROUNDING = {"f64_gauss_off1e6_C700", "f64_gauss_off1e6_C9000", "f64_exact_ties",
+                  "f64_mag1e200_C64", "f64_mag1e200_C5000"}
+
+
+def _grad64(name, tag, shape):
+    g = np.zeros(shape, np.float64)
+    g[GOLDEN64[f"{name}/{tag}_r"], GOLDEN64[f"{name}/{tag}_c"]] = GOLDEN64[f"{name}/{tag}_v"]
+    return g
+
+
+@pytest.mark.parametrize("name", NAMES64)
+def test_f64_oracle_matches_reference_outputs(name):
+    """The float64 restatement against the reference CPU kernel's float64
+    branch (exact fp64: same kappa, same gradient, loss to rounding) and
+    against reference_impl.FWLoss on float64 tensors (float32-rounded 1/k)."""
+    z, y = dict(cases.f64_cases())[name]()
+    B = len(y)
+    s = O.solve_f64(z, y, 1.0 / B)
+    np.testing.assert_array_equal(s["mask"].sum(1), s["kappa"])
+    np.testing.assert_array_equal(s["kappa"], GOLDEN64[f"{name}/kappa_cpu64"])
+    np.testing.assert_allclose(s["loss"], GOLDEN64[f"{name}/loss_cpu64"], rtol=1e-9, atol=1e-12)
+    np.testing.assert_allclose(s["grad"], _grad64(name, "grad_cpu64", z.shape), rtol=1e-15, atol=0)
+    if name not in REF64_ROUNDING:
+        np.testing.assert_array_equal(s["kappa"], GOLDEN64[f"{name}/kappa_ref64"])
+        np.testing.assert_allclose(s["H"], GOLDEN64[f"{name}/H_ref64"], rtol=1e-6, atol=1e-7)
+        np.testing.assert_allclose(s["grad"], _grad64(name, "grad_ref64", z.shape), rtol=1e-6, atol=1e-9)
+
+
+def test_f64_round_down_minus1():
+    M = np.array([0.0, 1.0, 2.5, 1e17 + 16, 2.0 ** 53 + 2, 1e300, -7.25, np.inf, -np.inf])
+    t0 = O.round_down_minus1_f64(M)
+    fin = np.isfinite(M)
+    # t0 <= M - 1 exactly, and the next float64 up is > M - 1
+    from fractions import Fraction
+    for m, t in zip(M[fin], t0[fin]):
+        assert Fraction(t) <= Fraction(m) - 1
+        assert Fraction(np.nextafter(t, np.inf)) > Fraction(m) - 1
+    assert np.isinf(t0[~fin]).all()
