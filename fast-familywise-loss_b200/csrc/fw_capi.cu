@@ -20,6 +20,7 @@
 #include "fw_device.cuh"
 #include "fw_f64.cuh"
 #include "fw_lmhead.cuh"
+#include "fw_lmhead_tc.cuh"
 #include "fw_shard.cuh"
 #include "fw_stream_tier.cuh"
 #include "fw_warp_tier.cuh"
@@ -180,6 +181,39 @@ cudaError_t launch_f64(const F64Args& a, cudaStream_t st) {
   const int64_t need = (a.B + rows_per_block - 1) / rows_per_block;
   const int64_t cap = (int64_t)sm_count() * occ;
   return launch(k, dim3((unsigned)(need < cap ? need : cap)), dim3(kF64Threads), 1, st, a);
+}
+
+// cuTensorMapEncodeTiled, looked up through the runtime so that the library
+// does not link the driver library itself.
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                                  CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                  CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// Row-major bf16 matrix [rows, cols] as 64-column x box_rows tiles with the
+// 128-byte swizzle (out-of-range elements read as zero).
+bool make_tile_map_bf16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kTcBK, box_rows};
+  const cuuint32_t elem[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, elem,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 int aux_grid(int64_t rows, int per_block) {
@@ -484,6 +518,56 @@ int fw_loss_reduce(const float* loss, int64_t B, double scale, float* out, void*
   if (!out || (B > 0 && !loss)) return FWB_E_POINTER;
   return launch_status(launch(fw_loss_reduce_kernel<float>, dim3(1), dim3(kReduceThreads), 1,
                               static_cast<cudaStream_t>(stream), loss, B, scale, out));
+}
+
+int fw_lmhead_fused_scan(int dtype, const void* hidden, int64_t B, int64_t D, const void* weight, int64_t C,
+                         int nchunks, const int64_t* col_start, int K, const int64_t* y, float* zy,
+                         int32_t* summaries, int32_t* local_idx, int32_t* status, void* stream) {
+  if (dtype != FWB_DTYPE_BF16) return FWB_E_DTYPE;
+  if (B < 0 || C < 1 || D < 8 || D % 8 != 0 || B > (int64_t)INT_MAX - kTcBM || C > (int64_t)INT_MAX - kTcBN ||
+      D > (int64_t)INT_MAX - kTcBK)
+    return FWB_E_SHAPE;
+  if (nchunks < 1 || nchunks > kMaxShards || K < 1 || K > kShardMaxK) return FWB_E_CAPACITY;
+  if (!col_start) return FWB_E_POINTER;
+  if (col_start[0] != 0 || col_start[nchunks] != C) return FWB_E_SHAPE;
+  for (int q = 0; q < nchunks; ++q)
+    if (col_start[q + 1] <= col_start[q] || col_start[q] % kTcBN != 0) return FWB_E_SHAPE;
+  if (B == 0) return FWB_OK;
+  if (!hidden || !weight || !y || !zy || !summaries || !local_idx) return FWB_E_POINTER;
+  if (!aligned16(hidden) || !aligned16(weight)) return FWB_E_SHAPE;
+  TcArgs a = {};
+  a.B = B;
+  a.C = C;
+  a.D = D;
+  a.nchunks = nchunks;
+  a.K = K;
+  a.n_mblocks = (int)((B + kTcBM - 1) / kTcBM);
+  for (int q = 0; q <= nchunks; ++q) a.col_start[q] = col_start[q];
+  a.y = y;
+  a.zy = zy;
+  a.summaries = summaries;
+  a.local_idx = local_idx;
+  a.status = status;
+  CUtensorMap tm_h, tm_w;
+  if (!make_tile_map_bf16(&tm_h, hidden, B, D, kTcBM) || !make_tile_map_bf16(&tm_w, weight, C, D, kTcBN))
+    return FWB_E_LAUNCH;
+  static bool attr_set[kMaxDevices] = {false};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return FWB_E_LAUNCH;
+  if (dev < kMaxDevices && !attr_set[dev]) {
+    if (cudaFuncSetAttribute(fw_lmhead_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kTcSmemBytes) != cudaSuccess)
+      return FWB_E_LAUNCH;
+    attr_set[dev] = true;
+  }
+  const int64_t nwork = (int64_t)a.n_mblocks * nchunks;
+  const int64_t sms = sm_count();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(nwork < sms ? nwork : sms));
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = kTcSmemBytes;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  return launch_status(cudaLaunchKernelEx(&cfg, fw_lmhead_tc_kernel, tm_h, tm_w, a));
 }
 
 int fw_loss_reduce_f64(const double* loss, int64_t B, double scale, double* out, void* stream) {

@@ -15,7 +15,7 @@
 //     so fw_backward needs no zero-initialised [N,K] buffer.
 // Extra functions used by the autograd layer (fwloss_b200 package):
 //   fused_fwd_bwd, scale_grad, loss_reduce, shard_scan, shard_solve, and the
-//   LM-head pieces shard_scan_into, label_logits, chunks_solve,
+//   LM-head pieces shard_scan_into, label_logits, lmhead_fused_scan, chunks_solve,
 //   sparse_grad_hidden, sparse_grad_weight.
 #include <torch/extension.h>
 
@@ -359,6 +359,40 @@ void label_logits(torch::Tensor z_chunk, torch::Tensor targets, int64_t c0, torc
            "fw_label_logits");
 }
 
+// LM head, fused form: the chunk summaries and label logits of
+// logits = hidden @ weight^T straight from the tensor-core GEMM (bf16 inputs),
+// into the given buffers; no logits are formed.
+void lmhead_fused_scan(torch::Tensor hidden, torch::Tensor weight, torch::Tensor targets,
+                       std::vector<int64_t> col_start, torch::Tensor summaries, torch::Tensor local_idx,
+                       torch::Tensor zy, c10::optional<torch::Tensor> status) {
+  TORCH_CHECK(hidden.is_cuda() && weight.is_cuda() && hidden.device() == weight.device(),
+              "hidden and weight must be CUDA tensors on one device");
+  TORCH_CHECK(hidden.scalar_type() == torch::kBFloat16 && weight.scalar_type() == torch::kBFloat16,
+              "the fused LM-head scan takes bfloat16 hidden and weight");
+  TORCH_CHECK(hidden.dim() == 2 && weight.dim() == 2 && hidden.size(1) == weight.size(1) &&
+                  hidden.is_contiguous() && weight.is_contiguous(),
+              "hidden [B, D] and weight [C, D] must be contiguous");
+  const c10::cuda::CUDAGuard guard(hidden.device());
+  const int64_t B = hidden.size(0), D = hidden.size(1), C = weight.size(0);
+  const int64_t n = (int64_t)col_start.size() - 1;
+  TORCH_CHECK(summaries.is_contiguous() && summaries.scalar_type() == torch::kInt32 && summaries.dim() == 3 &&
+                  summaries.size(0) == n && summaries.size(1) == B,
+              "summaries must be contiguous int32 [nchunks, B, 4 + K]");
+  const int64_t K = summaries.size(2) - 4;
+  TORCH_CHECK(local_idx.is_contiguous() && local_idx.scalar_type() == torch::kInt32 && local_idx.numel() == n * B * K,
+              "local_idx must be contiguous int32 [nchunks, B, K]");
+  TORCH_CHECK(zy.is_cuda() && zy.scalar_type() == torch::kFloat32 && zy.numel() == B && zy.is_contiguous(),
+              "zy must be a contiguous float32 [B] tensor");
+  check_targets(targets, B, hidden);
+  auto y = targets.contiguous();
+  int32_t* st = nullptr;
+  if (status.has_value()) st = status->data_ptr<int32_t>();
+  check_rc(fw_lmhead_fused_scan(FWB_DTYPE_BF16, hidden.data_ptr(), B, D, weight.data_ptr(), C, (int)n,
+                                col_start.data(), (int)K, y.data_ptr<int64_t>(), zy.data_ptr<float>(),
+                                summaries.data_ptr<int32_t>(), local_idx.data_ptr<int32_t>(), st, cur_stream()),
+           "fw_lmhead_fused_scan");
+}
+
 // (H, kappa, loss, sup_cols, fb_rows, fb_count) from the chunk summaries.
 std::vector<torch::Tensor> chunks_solve(torch::Tensor summaries, torch::Tensor local_idx,
                                         std::vector<int64_t> col_start, torch::Tensor zy, torch::Tensor targets,
@@ -466,6 +500,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("shard_scan", &shard_scan, "class-sharded step 1: local solve, zero gradient shard, summaries");
   m.def("shard_scan_into", &shard_scan_into, "summaries of one logit chunk into given buffers");
   m.def("label_logits", &label_logits, "zy[r] = chunk[r, y[r] - c0] for labels inside the chunk");
+  m.def("lmhead_fused_scan", &lmhead_fused_scan, "LM head: chunk summaries from the tensor-core GEMM",
+        py::arg("hidden"), py::arg("weight"), py::arg("targets"), py::arg("col_start"), py::arg("summaries"),
+        py::arg("local_idx"), py::arg("zy"), py::arg("status") = py::none());
   m.def("chunks_solve", &chunks_solve, "LM head: combine chunk summaries",
         py::arg("summaries"), py::arg("local_idx"), py::arg("col_start"), py::arg("zy"), py::arg("targets"),
         py::arg("status") = py::none());

@@ -47,6 +47,8 @@ _SIGS["fw_sparse_grad_weight"] = ([ctypes.c_int, _P, _I64, _I64, _P, ctypes.c_in
 _SIGS["fw_weight_grad_keys"] = ([_P, ctypes.c_int, _P, _P, _I64, _I64, _P, _P], ctypes.c_int)
 _SIGS["fw_segment_grad_weight"] = ([ctypes.c_int, _P, _I64, _I64, _P, _I64, _P, ctypes.c_float, _P,
                                    ctypes.c_int, _P, _P], ctypes.c_int)
+_SIGS["fw_lmhead_fused_scan"] = ([ctypes.c_int, _P, _I64, _I64, _P, _I64, ctypes.c_int, _P, ctypes.c_int, _P, _P,
+                                  _P, _P, _P, _P], ctypes.c_int)
 _SIGS["fw_fused_fwd_bwd_f64"] = ([_P, _P, _I64, _I64, _I64, ctypes.c_double, _P, _P, _P, _P, _P, _P],
                                  ctypes.c_int)
 _SIGS["fw_scale_grad_f64"] = ([_P, _P, ctypes.c_int, ctypes.c_double, _I64, _I64, _I64, _P], ctypes.c_int)

@@ -24,6 +24,12 @@ deterministic and only touched rows are written.
 Rows where a chunk's own support exceeds K entries (near-constant logits) are
 solved exactly from their full logit rows, and their gradient rows are
 applied densely; counting them costs one 4-byte device-to-host read per step.
+
+impl="fused" (bf16 only) replaces the chunk GEMMs and scans by one
+tensor-core kernel (fw_lmhead_fused_scan, sm_100a tcgen05) whose epilogue
+writes the same chunk summaries straight from the accumulators: no logit
+chunk is written to memory.  impl="staged" is the GEMM + scan form above;
+impl="auto" picks the fused kernel where it applies.
 """
 import torch
 
@@ -31,6 +37,23 @@ from ._native import ext
 from .sharded import even_col_start
 
 DEFAULT_K = 16
+FUSED_TILE = 256  # column tile of the fused kernel: chunk starts are multiples of it
+DEFAULT_IMPL = "staged"
+STATUS_TIMEOUT = 4
+
+
+def tile_col_start(num_classes, nchunks, tile=FUSED_TILE):
+    """Chunk offsets whose starts are multiples of `tile` (at most nchunks
+    chunks, fewer when the classes do not fill them)."""
+    C = int(num_classes)
+    width = -(-(-(-C // int(nchunks))) // tile) * tile
+    return list(range(0, C, width)) + [C]
+
+
+def _fused_ok(hidden, weight):
+    return (hidden.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 and hidden.shape[1] % 8 == 0
+            and hidden.data_ptr() % 16 == 0 and weight.data_ptr() % 16 == 0
+            and torch.cuda.get_device_capability(hidden.device) == (10, 0))
 
 
 def _logits_chunk(hidden, w_chunk):
@@ -54,36 +77,45 @@ def _full_logits(hidden_rows, weight):
 
 class _FWLMHead(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, hidden, weight, target, scale, nchunks, K):
+    def forward(ctx, hidden, weight, target, scale, nchunks, K, fused):
         fw = ext()
         B = hidden.shape[0]
         C = weight.shape[0]
-        col_start = even_col_start(C, nchunks)
+        col_start = tile_col_start(C, nchunks) if fused else even_col_start(C, nchunks)
+        nchunks = len(col_start) - 1
         dev = hidden.device
         summaries = torch.empty((nchunks, B, 4 + K), dtype=torch.int32, device=dev)
         local_idx = torch.empty((nchunks, B, K), dtype=torch.int32, device=dev)
         zy = torch.empty(B, dtype=torch.float32, device=dev)
-        # The GEMM of chunk q+1 (tensor cores) runs while chunk q is being
-        # summarised on a second stream (HBM-bound); a chunk's memory is
-        # released only after its scan (record_stream).
-        main = torch.cuda.current_stream(dev)
-        side = _side_stream(dev)
-        side.wait_stream(main)
-        for q in range(nchunks):
-            c0, c1 = col_start[q], col_start[q + 1]
-            z = _logits_chunk(hidden, weight[c0:c1])
-            ready = torch.cuda.Event()
-            ready.record(main)
-            with torch.cuda.stream(side):
-                side.wait_event(ready)
-                fw.shard_scan_into(z, K, summaries[q], local_idx[q])
-                fw.label_logits(z, target, c0, zy)
-            z.record_stream(side)
-            del z
-        main.wait_stream(side)
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        if fused:
+            fw.lmhead_fused_scan(hidden, weight, target, col_start, summaries, local_idx, zy, status)
+        else:
+            # The GEMM of chunk q+1 (tensor cores) runs while chunk q is being
+            # summarised on a second stream (HBM-bound); a chunk's memory is
+            # released only after its scan (record_stream).
+            main = torch.cuda.current_stream(dev)
+            side = _side_stream(dev)
+            side.wait_stream(main)
+            for q in range(nchunks):
+                c0, c1 = col_start[q], col_start[q + 1]
+                z = _logits_chunk(hidden, weight[c0:c1])
+                ready = torch.cuda.Event()
+                ready.record(main)
+                with torch.cuda.stream(side):
+                    side.wait_event(ready)
+                    fw.shard_scan_into(z, K, summaries[q], local_idx[q])
+                    fw.label_logits(z, target, c0, zy)
+                z.record_stream(side)
+                del z
+            main.wait_stream(side)
         H, kappa, loss_rows, sup_cols, fb_rows, fb_count = fw.chunks_solve(summaries, local_idx, col_start, zy, target)
         out = fw.loss_reduce(loss_rows, float(scale))
-        nfb = int(fb_count.item())  # read after the step's work is queued
+        # one read after the step's work is queued: exact-path row count and
+        # the fused kernel's status word
+        nfb, st = torch.cat([fb_count, status]).tolist()
+        if st & STATUS_TIMEOUT:
+            raise RuntimeError("fw_lmhead_fused_scan: a bounded on-chip wait timed out")
         rows = g_rows = None
         if nfb:  # rare: rows solved from their full logit rows; their losses were 0 in `out`
             rows = fb_rows[:nfb].long().sort().values
@@ -114,17 +146,22 @@ class _FWLMHead(torch.autograd.Function):
                 dH[ctx.rows] = (gr @ weight.float()).to(dH.dtype)
             if dW is not None:
                 dW += (gr.t() @ hidden[ctx.rows].float()).to(dW.dtype)
-        return dH, dW, None, None, None, None
+        return dH, dW, None, None, None, None, None
 
 
-def fw_lm_head_loss(hidden, weight, target, reduction="mean", nchunks=None, K=DEFAULT_K):
+def fw_lm_head_loss(hidden, weight, target, reduction="mean", nchunks=None, K=DEFAULT_K, impl=None):
     """Mean/sum FW loss of logits = hidden @ weight^T.
 
     hidden [B, D] and weight [C, D]: CUDA, both float32 or both bfloat16;
     target [B] int64.  `nchunks` column chunks (default: chunks of ~16k
-    classes, at most 16) bound the logit memory to B x C / nchunks fp32."""
+    classes, at most 16) bound the logit memory to B x C / nchunks fp32
+    (staged form).  impl: "staged", "fused" (bf16, sm_100a; raises where it
+    does not apply) or "auto" (fused where it applies); default DEFAULT_IMPL."""
     if reduction not in ("mean", "sum"):
         raise ValueError(f"Invalid reduction mode: {reduction}")
+    impl = DEFAULT_IMPL if impl is None else impl
+    if impl not in ("staged", "fused", "auto"):
+        raise ValueError(f"Invalid impl: {impl}")
     if not (hidden.is_cuda and weight.is_cuda and hidden.dim() == 2 and weight.dim() == 2):
         raise TypeError("fw_lm_head_loss: hidden [B, D] and weight [C, D] must be CUDA matrices")
     if hidden.dtype != weight.dtype or hidden.dtype not in (torch.float32, torch.bfloat16):
@@ -137,4 +174,9 @@ def fw_lm_head_loss(hidden, weight, target, reduction="mean", nchunks=None, K=DE
     nchunks = max(1, min(int(nchunks), C, 16, 256 // int(K)))
     B = hidden.shape[0]
     scale = (1.0 / B if B else float("nan")) if reduction == "mean" else 1.0
-    return _FWLMHead.apply(hidden.contiguous(), weight.contiguous(), target, scale, nchunks, int(K))
+    hidden, weight = hidden.contiguous(), weight.contiguous()
+    fused = impl != "staged" and _fused_ok(hidden, weight)
+    if impl == "fused" and not fused:
+        raise TypeError("fw_lm_head_loss(impl='fused'): needs bfloat16 hidden/weight, D % 8 == 0, "
+                        "16-byte aligned data and an sm_100 GPU")
+    return _FWLMHead.apply(hidden, weight, target, scale, nchunks, int(K), fused)

@@ -56,6 +56,7 @@ extern "C" {
 
 #define FWB_STATUS_LABEL_RANGE 1   /* some label y[r] is outside [0, C)          */
 #define FWB_STATUS_NONFINITE 2     /* some row maximum is NaN or +-inf           */
+#define FWB_STATUS_TIMEOUT 4       /* a bounded on-chip wait gave up (fused LM-head kernel) */
 
 /* Library version, "major.minor.patch". */
 FWB_API const char* fw_version(void);
@@ -223,6 +224,25 @@ FWB_API int fw_shard_solve(const int32_t* gathered, int nranks, int rank,
  */
 FWB_API int fw_label_logits(const float* z, int64_t B, int64_t C, int64_t ld, const int64_t* y,
                             int64_t c0, float* zy, void* stream);
+
+/*
+ * LM-head chunk summaries straight from the GEMM (sm_100a tensor cores):
+ * logits = hidden [B, D] x weight [C, D]^T (bf16, row-major, D % 8 == 0,
+ * 16-byte aligned bases) are accumulated in tensor memory and reduced to the
+ * chunk summary records that fw_shard_scan writes from stored logits
+ * (summaries [nchunks, B, 4 + K], local_idx [nchunks, B, K]), plus the label
+ * logit zy[r] = logits[r, y[r]]; no logit is written to memory.  col_start
+ * (host, nchunks + 1 entries) starts every chunk at a multiple of 256 columns
+ * and ends at C.  A chunk whose candidates overflow the on-chip list is
+ * recorded with kappa = K + 1 (the row then takes the exact full-row path in
+ * fw_chunks_solve).  Status bit FWB_STATUS_TIMEOUT reports a bounded on-chip
+ * wait that gave up.  No counterpart in the reference: the fused form of
+ * logits = hidden @ W^T followed by FWLoss (reference_impl.py:11-26).
+ */
+FWB_API int fw_lmhead_fused_scan(int dtype, const void* hidden, int64_t B, int64_t D, const void* weight,
+                                 int64_t C, int nchunks, const int64_t* col_start, int K,
+                                 const int64_t* y, float* zy, int32_t* summaries, int32_t* local_idx,
+                                 int32_t* status, void* stream);
 
 FWB_API int fw_chunks_solve(const int32_t* summaries, const int32_t* local_idx, int nchunks,
                             const int64_t* col_start, int64_t B, int K, const float* zy,
