@@ -49,7 +49,7 @@ def build_lib(force=False, verbose=False):
         return LIB
     cmd = [_nvcc(), *NVCC_ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
            "-Xcompiler", "-fvisibility=hidden", "-shared", "-o", LIB + ".tmp",
-           os.path.join(CSRC, "fw_capi.cu")]
+           os.path.join(CSRC, "fw_capi.cu"), os.path.join(CSRC, "fw_noalloc.cu")]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     subprocess.run(cmd, check=True)

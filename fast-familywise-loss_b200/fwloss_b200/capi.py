@@ -53,6 +53,8 @@ _SIGS["fw_fused_fwd_bwd_f64"] = ([_P, _P, _I64, _I64, _I64, ctypes.c_double, _P,
                                  ctypes.c_int)
 _SIGS["fw_scale_grad_f64"] = ([_P, _P, ctypes.c_int, ctypes.c_double, _I64, _I64, _I64, _P], ctypes.c_int)
 _SIGS["fw_loss_reduce_f64"] = ([_P, _I64, ctypes.c_double, _P, _P], ctypes.c_int)
+_SIGS["fw_lmhead_fused_loss_noalloc"] = ([ctypes.c_int, _P, _I64, _I64, _P, _I64, ctypes.c_int, _P, ctypes.c_int,
+                                          _P, _P, _P, _P, _P, _P, _P, _P, _P], ctypes.c_int)
 DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 _ANY_FLOAT = (torch.float32, torch.bfloat16, torch.float16, torch.float64)
 

@@ -313,6 +313,32 @@ FWB_API int fw_scale_grad_f64(double* grad, const double* grad_output, int per_r
 FWB_API int fw_loss_reduce_f64(const double* loss, int64_t B, double scale, double* out,
                                void* stream);
 
+/*
+ * LM-head forward in one call that allocates nothing: fw_lmhead_fused_scan
+ * followed by fw_chunks_solve (same arguments, outputs and limits as those
+ * two), with their workspace -- the chunk summaries, the support's local
+ * columns and the label logits -- kept in a fixed array inside the library
+ * instead of buffers from the caller.  For callers that cannot call
+ * cudaMalloc: plugins whose host framework owns all device memory, servers
+ * that forbid allocation after start-up, FFI hosts that only hold the buffers
+ * handed to them.  The workspace needs
+ *     round_up(nchunks * B * (4 + K), 64) + round_up(nchunks * B * K, 64) + B
+ * 4-byte words, at most FWB_NOALLOC_SCRATCH_BYTES / 4; larger problems
+ * return FWB_E_CAPACITY (e.g. B = 8192, nchunks = 8, K = 16 fits).  The array
+ * is FWB_NOALLOC_SCRATCH_BYTES on every GPU that loads the library, held until
+ * exit.  The first call on a device looks up the array's address with that
+ * device current; make it before any stream capture.  All calls share the
+ * array: calls that overlap on the GPU race.  No counterpart in the reference.
+ */
+#define FWB_NOALLOC_SCRATCH_BYTES (16 * 1024 * 1024)
+
+FWB_API int fw_lmhead_fused_loss_noalloc(int dtype, const void* hidden, int64_t B, int64_t D,
+                                         const void* weight, int64_t C, int nchunks,
+                                         const int64_t* col_start, int K, const int64_t* y,
+                                         float* H, int32_t* kappa, float* loss, int32_t* sup_cols,
+                                         int32_t* fb_rows, int32_t* fb_count, int32_t* status,
+                                         void* stream);
+
 #ifdef __cplusplus
 }
 #endif
