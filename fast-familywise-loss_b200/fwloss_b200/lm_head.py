@@ -29,7 +29,9 @@ impl="fused" (bf16 only) replaces the chunk GEMMs and scans by one
 tensor-core kernel (fw_lmhead_fused_scan, sm_100a tcgen05) whose epilogue
 writes the same chunk summaries straight from the accumulators: no logit
 chunk is written to memory.  impl="staged" is the GEMM + scan form above;
-impl="auto" picks the fused kernel where it applies.
+impl="auto" (the default) picks the fused kernel where it applies (B200,
+B = 8192, D = 4096, C = 128256: 7.45 ms per forward+backward fused, 8.77 ms
+staged).
 """
 import torch
 
@@ -38,16 +40,47 @@ from .sharded import even_col_start
 
 DEFAULT_K = 16
 FUSED_TILE = 256  # column tile of the fused kernel: chunk starts are multiples of it
-DEFAULT_IMPL = "staged"
+DEFAULT_IMPL = "auto"
 STATUS_TIMEOUT = 4
 
 
 def tile_col_start(num_classes, nchunks, tile=FUSED_TILE):
-    """Chunk offsets whose starts are multiples of `tile` (at most nchunks
-    chunks, fewer when the classes do not fill them)."""
+    """Chunk offsets whose starts are multiples of `tile`: the column tiles
+    are dealt out evenly (chunk sizes differ by at most one tile), at most
+    nchunks chunks, fewer when there are fewer tiles."""
     C = int(num_classes)
-    width = -(-(-(-C // int(nchunks))) // tile) * tile
-    return list(range(0, C, width)) + [C]
+    tiles = -(-C // tile)
+    n = max(1, min(int(nchunks), tiles))
+    base, extra = divmod(tiles, n)
+    out, t = [0], 0
+    for q in range(n):
+        t += base + (1 if q < extra else 0)
+        out.append(min(t * tile, C))
+    return out
+
+
+def fused_nchunks(batch, num_classes, sms, max_chunks=16, tile=FUSED_TILE):
+    """Chunk count for the fused kernel.  Its persistent CTAs (one per SM)
+    take (128-row block, chunk) work items of equal size round-robin, so the
+    last round leaves SMs idle unless the item count is close to a multiple
+    of the SM count: pick the count in [1, max_chunks] with the best filled
+    fraction of the rounds, the largest such count on ties (within 1 %):
+    smaller items also keep the weight columns that run concurrently in L2
+    (B200, B = 8192, C = 128256: 16 chunks 6.4 ms, 9 chunks 6.85 ms, both
+    97 % filled)."""
+    mblocks = -(-int(batch) // 128)
+    tiles = -(-int(num_classes) // tile)
+    best, best_eff = 1, -1.0
+    for n in range(1, max(1, min(max_chunks, tiles)) + 1):
+        items = mblocks * n
+        per_item = -(-tiles // n)  # the largest item's tiles
+        rounds = -(-items // sms)
+        eff = (mblocks * tiles) / (rounds * sms * per_item)
+        if eff >= best_eff - 0.01:
+            if eff > best_eff:
+                best_eff = eff
+            best = n
+    return best
 
 
 def _fused_ok(hidden, weight):
@@ -169,9 +202,6 @@ def fw_lm_head_loss(hidden, weight, target, reduction="mean", nchunks=None, K=DE
     if hidden.shape[1] != weight.shape[1]:
         raise ValueError("fw_lm_head_loss: hidden and weight disagree on D")
     C = weight.shape[0]
-    if nchunks is None:
-        nchunks = max(1, min(16, -(-C // 16384)))
-    nchunks = max(1, min(int(nchunks), C, 16, 256 // int(K)))
     B = hidden.shape[0]
     scale = (1.0 / B if B else float("nan")) if reduction == "mean" else 1.0
     hidden, weight = hidden.contiguous(), weight.contiguous()
@@ -179,4 +209,11 @@ def fw_lm_head_loss(hidden, weight, target, reduction="mean", nchunks=None, K=DE
     if impl == "fused" and not fused:
         raise TypeError("fw_lm_head_loss(impl='fused'): needs bfloat16 hidden/weight, D % 8 == 0, "
                         "16-byte aligned data and an sm_100 GPU")
+    if nchunks is None:
+        if fused:
+            sms = torch.cuda.get_device_properties(hidden.device).multi_processor_count
+            nchunks = fused_nchunks(B, C, sms, max_chunks=min(16, 256 // int(K)))
+        else:
+            nchunks = max(1, min(16, -(-C // 16384)))
+    nchunks = max(1, min(int(nchunks), C, 16, 256 // int(K)))
     return _FWLMHead.apply(hidden, weight, target, scale, nchunks, int(K), fused)

@@ -39,7 +39,7 @@ def test_lm_head_matches_dense(dtype, tol, B, D, C, nchunks):
     ref_loss, ref_dh, ref_dw, z = dense_reference(hidden, weight, target, "mean")
     h = hidden.clone().requires_grad_(True)
     w = weight.clone().requires_grad_(True)
-    loss = fw_lm_head_loss(h, w, target, reduction="mean", nchunks=nchunks)
+    loss = fw_lm_head_loss(h, w, target, reduction="mean", nchunks=nchunks, impl="staged")
     loss.backward()
     assert h.grad.dtype == dtype and w.grad.dtype == dtype
     np.testing.assert_allclose(loss.float().item(), ref_loss.item(), rtol=1e-5 if dtype == torch.float32 else 1e-2)
@@ -58,7 +58,7 @@ def test_lm_head_rows_needing_the_exact_path():
     ref_loss, ref_dh, ref_dw, _ = dense_reference(hidden, weight, target, "sum")
     h = hidden.clone().requires_grad_(True)
     w = weight.clone().requires_grad_(True)
-    loss = fw_lm_head_loss(h, w, target, reduction="sum", nchunks=4, K=8)
+    loss = fw_lm_head_loss(h, w, target, reduction="sum", nchunks=4, K=8, impl="staged")
     (3.0 * loss).backward()
     np.testing.assert_allclose(loss.item(), ref_loss.item(), rtol=1e-5)
     np.testing.assert_allclose(h.grad.cpu().numpy(), 3.0 * ref_dh.cpu().numpy(), rtol=2e-5, atol=1e-6)
