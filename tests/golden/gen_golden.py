@@ -6,7 +6,11 @@ Run in a container that has the reference checkout (FW_REF_PATH, default
     python tests/golden/gen_golden.py
 
 Outputs (inputs are not stored: every case regenerates them from its seed,
-see tests/cases.py and fwloss_b200.workloads):
+see tests/cases.py and fwloss_b200.workloads; each case records the sha256 of
+the regenerated inputs as `<case>/input_sha256`, so that a test on another
+host can tell whether its inputs are the ones these outputs were made from --
+torch's CPU normal generator gives different float32 values on hosts that run
+its scalar kernels instead of the AVX2/AVX-512 ones):
   reference_outputs.npz  per case: what reference_impl.FWLoss (float32, CPU;
                          reference_impl.py:3-35) and the reference CPU
                          extension (src/cpu/fw_cpu.cpp, fw_loss_grad) return:
@@ -23,6 +27,7 @@ see tests/cases.py and fwloss_b200.workloads):
                          with the generation parameters of
                          benchmarks/cpu_benchmarks/bench_cpu_e2e.py:7-41.
 """
+import hashlib
 import json
 import os
 import sys
@@ -45,6 +50,10 @@ from oracle import ref_cpu  # noqa: E402
 import reference_impl  # noqa: E402  (the reference's own module)
 
 CONFIG_ROWS = {"cfg0": 256, "cfg1": 512, "cfg2": 64, "cfg3": 2048, "cfg4": 8}
+
+
+def input_sha256(z, y):
+    return np.array(hashlib.sha256(np.ascontiguousarray(z).tobytes() + np.ascontiguousarray(y).tobytes()).hexdigest())
 
 
 def sparse(g):
@@ -126,6 +135,7 @@ def main():
         z, y = gen()
         for k, v in reference_outputs(z, y).items():
             store[f"{name}/{k}"] = v
+        store[f"{name}/input_sha256"] = input_sha256(z, y)
         print(name, z.shape, flush=True)
     np.savez_compressed(os.path.join(HERE, "reference_outputs.npz"), **store)
     store64 = {}
@@ -133,6 +143,7 @@ def main():
         z, y = gen()
         for k, v in reference_outputs_f64(z, y).items():
             store64[f"{name}/{k}"] = v
+        store64[f"{name}/input_sha256"] = input_sha256(z, y)
         print(name, z.shape, flush=True)
     np.savez_compressed(os.path.join(HERE, "reference_outputs_f64.npz"), **store64)
     with open(os.path.join(HERE, "kat_kbar.json"), "w") as f:

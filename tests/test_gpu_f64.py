@@ -63,6 +63,7 @@ def test_f64_matches_oracle_and_reference(name, gen):
     out = _fused64(z, y, scale)
     _check(out, ref, name)
     assert out["status"] == 0
+    assert cases.golden_inputs_match(GOLDEN64, name, z, y), f"{name}: inputs differ from the golden fixtures'"
     np.testing.assert_array_equal(out["kappa"], GOLDEN64[f"{name}/kappa_cpu64"], err_msg="kappa vs ref CPU")
     np.testing.assert_allclose(out["loss"], GOLDEN64[f"{name}/loss_cpu64"], rtol=1e-9, atol=1e-12)
     g = np.zeros(z.shape, np.float64)

@@ -40,6 +40,10 @@ NAMES = sorted({k.split("/")[0] for k in GOLDEN.files})
 @pytest.mark.parametrize("name", NAMES)
 def test_oracle_matches_reference_outputs(name):
     z, y = _inputs(name)
+    if name in CONFIG_ROWS and not cases.golden_inputs_match(GOLDEN, name, z, y):
+        pytest.skip(f"{name}: torch's CPU generator gives other inputs on this host than on the one that "
+                    "made the fixtures")
+    assert cases.golden_inputs_match(GOLDEN, name, z, y), f"{name}: inputs differ from the golden fixtures'"
     B = len(y)
     s = O.solve(z, y, 1.0 / B)
     np.testing.assert_array_equal(s["kappa"], GOLDEN[f"{name}/kappa_cpu"])
