@@ -3,6 +3,8 @@
 // reduction.  All are HBM-streaming kernels (no tensor-core work).
 #pragma once
 
+#include <cooperative_groups.h>
+
 #include "fw_device.cuh"
 
 namespace fwb200 {
@@ -140,24 +142,100 @@ __global__ void __launch_bounds__(kAuxThreads)
   }
 }
 
-// out[0] = scale * sum(loss[0..B)), fp64 accumulation in a fixed order (one
-// CTA; thread t sums t, t + 1024, ...; then a fixed tree).  T: fp32 or fp64
-// losses and result.
-constexpr int kReduceThreads = 1024;
+// out[0] = scale * sum(loss[0..B)) with fp64 accumulation in a fixed order,
+// by CL CTAs (one thread-block cluster when CL > 1): CTA r owns the r-th of
+// CL equal slices of the 16-byte groups of `loss`; thread t of a CTA sums
+// the groups t, t + T, t + 2T, ... of its slice (values in index order inside
+// a group, kReduceBatch groups loaded before they are added, so that each
+// thread keeps several loads in flight), then a fixed butterfly and a fixed
+// tree over the warps give the CTA's partial; CTA 0 adds the partials in rank
+// order through distributed shared memory.  Large batches use CL = 8 (eight
+// SMs keep eight times the loads of one in flight; the losses are read from
+// L2), small ones CL = 1 (a cluster launch costs about a microsecond more).
+// The choice and the partition depend only on B, so the result is
+// deterministic.  `vec`: loss is 16-byte aligned; otherwise scalar loads in
+// the same order.
+//
+// The kernel is launched as a programmatic dependent of the kernel before it
+// on the stream (usually the one that wrote the losses): it may be scheduled
+// while that kernel drains, and griddepcontrol.wait holds every thread until
+// that kernel has completed and its writes are visible.  T: fp32 or fp64.
+constexpr int kReduceCluster = 8;
+constexpr int64_t kReduceClusterMinRows = 16384;  // B above which CL = kReduceCluster
+constexpr int kReduceThreads = 512;
+constexpr int kReduceBatch = 4;  // 16-byte loads in flight per thread
+
+// Sixteen bytes of T (four floats or two doubles) per load.
 template <class T>
+struct Vec16;
+template <>
+struct Vec16<float> {
+  static constexpr int N = 4;
+  __device__ static void load(const float* p, double (&v)[4]) {
+    const float4 x = *reinterpret_cast<const float4*>(p);
+    v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+  }
+};
+template <>
+struct Vec16<double> {
+  static constexpr int N = 2;
+  __device__ static void load(const double* p, double (&v)[2]) {
+    const double2 x = *reinterpret_cast<const double2*>(p);
+    v[0] = x.x; v[1] = x.y;
+  }
+};
+
+template <class T, int CL>
 __global__ void __launch_bounds__(kReduceThreads)
     fw_loss_reduce_kernel(const T* __restrict__ loss, int64_t B,
-                          double scale, T* __restrict__ out) {
+                          double scale, T* __restrict__ out, int vec) {
+  constexpr int N = Vec16<T>::N;
   __shared__ double part[kReduceThreads / 32];
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  int rank = 0;
+  if constexpr (CL > 1) rank = (int)cooperative_groups::this_cluster().block_rank();
+  const int64_t ngroups = (B + N - 1) / N;
+  const int64_t g_lo = ngroups * rank / CL;
+  const int64_t g_hi = ngroups * (rank + 1) / CL;
   double s = 0.0;
-  for (int64_t i = threadIdx.x; i < B; i += kReduceThreads) s += (double)loss[i];
+  for (int64_t g0 = g_lo + threadIdx.x; g0 < g_hi; g0 += (int64_t)kReduceThreads * kReduceBatch) {
+    double v[kReduceBatch][N];
+#pragma unroll
+    for (int k = 0; k < kReduceBatch; ++k) {
+      const int64_t g = g0 + (int64_t)k * kReduceThreads;
+      const int64_t i0 = g * N;
+      if (vec && g < g_hi && i0 + N <= B) {
+        Vec16<T>::load(loss + i0, v[k]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < N; ++j) v[k][j] = (g < g_hi && i0 + j < B) ? (double)loss[i0 + j] : 0.0;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kReduceBatch; ++k)
+#pragma unroll
+      for (int j = 0; j < N; ++j) s += v[k][j];
+  }
   s = warp_sum(s);
   if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
   __syncthreads();
   if (threadIdx.x < 32) {
-    double t = part[threadIdx.x];
+    double t = (threadIdx.x < kReduceThreads / 32) ? part[threadIdx.x] : 0.0;
     t = warp_sum(t);
-    if (threadIdx.x == 0) out[0] = (T)(t * scale);
+    if (threadIdx.x == 0) {
+      if constexpr (CL == 1) out[0] = (T)(t * scale);
+      part[0] = t;
+    }
+  }
+  if constexpr (CL > 1) {
+    auto cluster = cooperative_groups::this_cluster();
+    cluster.sync();  // every CTA's partial is in its part[0]
+    if (rank == 0 && threadIdx.x == 0) {
+      double t = 0.0;
+      for (int r = 0; r < CL; ++r) t += *cluster.map_shared_rank(&part[0], r);
+      out[0] = (T)(t * scale);
+    }
+    cluster.sync();  // the partials stay readable until CTA 0 has read them
   }
 }
 

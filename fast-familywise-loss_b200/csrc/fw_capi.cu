@@ -47,6 +47,30 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 int launch_status(cudaError_t e) { return e == cudaSuccess ? FWB_OK : FWB_E_LAUNCH; }
 
+// The loss reduction: one CTA, or one cluster of kReduceCluster CTAs above
+// kReduceClusterMinRows rows, launched as a programmatic dependent of the
+// previous kernel on the stream.
+template <class T>
+cudaError_t launch_loss_reduce(const T* loss, int64_t B, double scale, T* out, cudaStream_t st) {
+  const bool cl = B > kReduceClusterMinRows;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cl ? kReduceCluster : 1);
+  cfg.blockDim = dim3(kReduceThreads);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = kReduceCluster;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = cl ? 2 : 1;
+  const int vec = aligned16(loss) ? 1 : 0;
+  return cl ? cudaLaunchKernelEx(&cfg, fw_loss_reduce_kernel<T, kReduceCluster>, loss, B, scale, out, vec)
+            : cudaLaunchKernelEx(&cfg, fw_loss_reduce_kernel<T, 1>, loss, B, scale, out, vec);
+}
+
 template <class... KArgs, class... Args>
 cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, int cluster,
                    cudaStream_t stream, Args&&... args) {
@@ -516,8 +540,7 @@ int fw_segment_grad_weight(int dtype, const void* hidden, int64_t B, int64_t D, 
 int fw_loss_reduce(const float* loss, int64_t B, double scale, float* out, void* stream) {
   if (B < 0) return FWB_E_SHAPE;
   if (!out || (B > 0 && !loss)) return FWB_E_POINTER;
-  return launch_status(launch(fw_loss_reduce_kernel<float>, dim3(1), dim3(kReduceThreads), 1,
-                              static_cast<cudaStream_t>(stream), loss, B, scale, out));
+  return launch_status(launch_loss_reduce<float>(loss, B, scale, out, static_cast<cudaStream_t>(stream)));
 }
 
 int fw_lmhead_fused_scan(int dtype, const void* hidden, int64_t B, int64_t D, const void* weight, int64_t C,
@@ -573,8 +596,7 @@ int fw_lmhead_fused_scan(int dtype, const void* hidden, int64_t B, int64_t D, co
 int fw_loss_reduce_f64(const double* loss, int64_t B, double scale, double* out, void* stream) {
   if (B < 0) return FWB_E_SHAPE;
   if (!out || (B > 0 && !loss)) return FWB_E_POINTER;
-  return launch_status(launch(fw_loss_reduce_kernel<double>, dim3(1), dim3(kReduceThreads), 1,
-                              static_cast<cudaStream_t>(stream), loss, B, scale, out));
+  return launch_status(launch_loss_reduce<double>(loss, B, scale, out, static_cast<cudaStream_t>(stream)));
 }
 
 int fw_fused_fwd_bwd_f64(const double* z, const int64_t* y, int64_t B, int64_t C, int64_t ld,

@@ -291,6 +291,15 @@ __device__ __forceinline__ float row_loss(float M, double tau, float zy) {
   return (float)(1.0 + ((double)M - (double)zy) + tau);
 }
 
+// Lets the kernel launched after this one on the stream as a programmatic
+// dependent (the loss reduction) be scheduled before this grid ends; the
+// dependent still waits (griddepcontrol.wait) for this grid to complete and
+// its writes to be visible before it reads anything.  A no-op when the next
+// launch is an ordinary one.
+__device__ __forceinline__ void allow_dependent_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void raise_status(int32_t* status, int bits) {
   if (status) atomicOr(reinterpret_cast<int*>(status), bits);
 }

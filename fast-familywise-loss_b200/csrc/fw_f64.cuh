@@ -164,6 +164,7 @@ __device__ __forceinline__ void f64_team_sync() {
 
 template <int TW, bool VEC>
 __global__ void __launch_bounds__(kF64Threads) fw_f64_rows_kernel(F64Args a) {
+  allow_dependent_launch();
   constexpr int NT = 32 * TW;          // threads per row
   constexpr int RPB = kF64Warps / TW;  // rows per CTA
   constexpr int W = VEC ? 2 : 1;       // doubles per item

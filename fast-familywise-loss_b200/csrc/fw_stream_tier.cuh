@@ -53,7 +53,15 @@ constexpr int kST = 256;              // threads per CTA
 constexpr int kSW = kST / 32;         // warps per CTA
 constexpr int kStreamListCap = 128;   // candidates per warp list
 constexpr int kSolveCap = 1024;       // gathered candidates per row
-constexpr int kStreamValues = 16;     // values per thread per streaming step
+constexpr int kStreamItems = 4;       // 16-byte loads per thread per streaming step (VEC)
+constexpr int kStreamScalars = 16;    // scalar loads per thread per streaming step (!VEC)
+
+// Loads per thread per streaming step: four 16-byte loads in flight for every
+// element type (16 fp32 or 32 bf16/fp16 values), 16 scalars without VEC.
+template <bool VEC>
+__host__ __device__ constexpr int stream_ipt() {
+  return VEC ? kStreamItems : kStreamScalars;
+}
 
 struct __align__(16) StreamShared {
   float lz[kSW][kStreamListCap];
@@ -177,7 +185,7 @@ __device__ __forceinline__ void for_each_element(const T* zr, int64_t C,
   constexpr int EPS = Elem<T>::kEPS;
   const Segment g = row_segment<CS, VEC, EPS>(C, rank);
   constexpr int W = VEC ? EPS : 1;
-  constexpr int IPT = kStreamValues / W;
+  constexpr int IPT = stream_ipt<VEC>();
   for (int64_t base = g.i0; base < g.i1; base += (int64_t)kST * IPT) {
     float v[IPT * W];
 #pragma unroll
@@ -212,6 +220,7 @@ __device__ __forceinline__ void for_each_element(const T* zr, int64_t C,
 template <class T, int CS, bool VEC, int OUT>
 __global__ void __launch_bounds__(kST)
     fw_stream_rows_kernel(RowArgs a) {
+  allow_dependent_launch();
   static_assert(OUT == kOutGrad || sizeof(T) == 4, "mask/candidate/shard outputs are fp32-only");
   constexpr bool kZeroFill = (OUT == kOutGrad || OUT == kOutShard);
   constexpr int EPS = Elem<T>::kEPS;
@@ -237,7 +246,7 @@ __global__ void __launch_bounds__(kST)
 
   // ---------------------------------------------------------------- stream
   constexpr int W = VEC ? EPS : 1;
-  constexpr int IPT = kStreamValues / W;
+  constexpr int IPT = stream_ipt<VEC>();
   const Segment g = row_segment<CS, VEC, EPS>(C, rank);
   float run = -CUDART_INF_F;
   int wcnt = 0;

@@ -161,16 +161,20 @@ __device__ __forceinline__ void warp_tier_nonfinite(const RowArgs& a, int64_t ro
   }
 }
 
-// Resident CTAs per SM the register budget is sized for: 3 (85 registers) up
-// to 16 values per lane, 2 (128) at 32, 1 at 64.
+// Resident CTAs per SM the register budget is sized for: 4 (64 registers) up
+// to 32 values per lane, 1 at 64.  Short rows are latency-bound (a serial
+// chain per row: load, max, candidate scan, fp64 fixed point, write), so the
+// extra resident rows pay for the tighter register budget (B200: cfg3
+// 18.6 -> 17.2 us, cfg1 13.1 -> 12.0 us against 3 and 2 CTAs per SM).
 template <int NV>
 constexpr int warp_tier_min_blocks() {
-  return NV <= 16 ? 3 : (NV <= 32 ? 2 : 1);
+  return NV <= 32 ? 4 : 1;
 }
 
 template <class T, int G, int NS, bool VEC, int OUT, bool FULLV>
 __global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS * Elem<T>::kEPS>())
     fw_warp_rows_kernel(RowArgs a) {
+  allow_dependent_launch();
   constexpr int EPS = Elem<T>::kEPS;
   constexpr int NV = NS * EPS;          // register values per lane
   constexpr int RPW = 32 / G;           // rows per warp
