@@ -217,8 +217,12 @@ __device__ __forceinline__ void for_each_element(const T* zr, int64_t C,
   }
 }
 
+// Five resident CTAs per SM (<= 51 registers): 16-bit rows stream in half
+// the time of fp32 ones, so more CTAs are needed to cover each row's
+// exchange/solve/patch phase (B200, cfg2 shape: bf16 99.1 -> 97.0 us, fp32
+// unchanged; six CTAs were slower).
 template <class T, int CS, bool VEC, int OUT>
-__global__ void __launch_bounds__(kST)
+__global__ void __launch_bounds__(kST, 5)
     fw_stream_rows_kernel(RowArgs a) {
   allow_dependent_launch();
   static_assert(OUT == kOutGrad || sizeof(T) == 4, "mask/candidate/shard outputs are fp32-only");

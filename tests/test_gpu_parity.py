@@ -276,6 +276,39 @@ def test_half_precision_logits(dtype, name):
 
 
 @pytest.mark.parametrize("dtype", list(HALF_TYPES))
+@pytest.mark.parametrize("C", [100, 5000])
+def test_half_precision_subnormal_candidates(dtype, C):
+    """Rows whose candidates are subnormal numbers of the 16-bit type, in both
+    tiers (C = 100: register tier, C = 5000: streaming tier).  float16: a
+    maximum of 1.0 makes the candidate threshold 0, and the positive
+    subnormals (>= 2^-24, resolvable in the fp64 shifted sums) are
+    candidates.  bfloat16 subnormals (~1e-39) are below the fp64 resolution
+    of z - M next to M = 1, so there the maximum is itself a small normal
+    number and the subnormals sit within 1 of it."""
+    tdt, rtol = HALF_TYPES[dtype]
+    tiny = float(torch.finfo(tdt).smallest_normal) / 4  # a subnormal of the type
+    top = 1.0 if tdt == torch.float16 else float(torch.finfo(tdt).smallest_normal) * 8
+    rng = np.random.default_rng(C)
+    B = 6
+    z = np.full((B, C), -2.0, np.float32)
+    for r in range(B):
+        cols = rng.choice(C, size=3 + 5 * r, replace=False)
+        z[r, cols] = tiny * rng.integers(1, 4, size=cols.size)
+        z[r, cols[0]] = top
+    z = torch.from_numpy(z).to(tdt).float().numpy()  # exact in the type
+    y = rng.integers(0, C, B).astype(np.int64)
+    ref = O.solve(z, y, 1.0 / B)
+    assert (ref["kappa"] > 1).sum() >= B - 1  # the subnormals decide the support
+    zt = torch.from_numpy(z).to(tdt).cuda()
+    grad, H, loss, kappa = capi.fused_fwd_bwd(zt, torch.from_numpy(y).cuda(), 1.0 / B)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(kappa.cpu().numpy(), ref["kappa"])
+    np.testing.assert_array_equal((z > H.cpu().numpy()[:, None]), ref["mask"])
+    np.testing.assert_allclose(loss.cpu().numpy(), ref["loss"], rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(grad.float().cpu().numpy(), ref["grad"], rtol=rtol, atol=ATOL)
+
+
+@pytest.mark.parametrize("dtype", list(HALF_TYPES))
 def test_half_precision_autograd(dtype):
     from fwloss_b200 import familywise_loss
 
