@@ -657,6 +657,67 @@ def run_lm_head(a):
     return 0
 
 
+def run_lm_head_vocab_parallel(a):
+    """LM head + FW loss, fwd+bwd, vocabulary-parallel over N GPUs (torchrun):
+    every rank holds the same hidden [B, D] and labels and C/N weight rows
+    (bf16), and runs vocab_parallel_lm_head_loss (the fused tcgen05 kernel on
+    its rows, an all-gather of the chunk summaries, the combined solve, the
+    sparse backward with an fp32 all-reduce of dhidden).  Strong scaling: the
+    job is one B x C head per step whatever N is."""
+    import torch
+    import torch.distributed as dist
+
+    from fwloss_b200.sharded import even_col_start
+    from fwloss_b200.vocab_parallel import vocab_parallel_lm_head_loss
+
+    world = int(os.environ["WORLD_SIZE"])
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    B, D, C = (int(v) for v in a.lm_shape.split(","))
+    cs = even_col_start(C, world)
+    g = torch.Generator(device=dev).manual_seed(4)  # same hidden and labels on every rank
+    hidden = (torch.randn(B, D, generator=g, device=dev) / D ** 0.5 * 4).to(torch.bfloat16).requires_grad_(True)
+    target = torch.randint(0, C, (B,), generator=g, device=dev)
+    gw = torch.Generator(device=dev).manual_seed(1000 + rank)  # this rank's weight rows
+    weight = torch.randn(cs[rank + 1] - cs[rank], D, generator=gw, device=dev).to(torch.bfloat16).requires_grad_(True)
+    forms = [f.strip() for f in a.lm_forms.split(",") if f.strip() in ("fused", "staged")] or ["fused"]
+    impl = forms[0]
+
+    def step():
+        hidden.grad = weight.grad = None
+        vocab_parallel_lm_head_loss(hidden, weight, target, cs, impl=impl).backward()
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(a.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item()) / a.steps
+    if rank == 0:
+        print(json.dumps({
+            "metric": f"LM head + FWLoss fwd+bwd rows/s (B={B}, D={D}, C={C}, bf16), vocabulary-parallel",
+            "value": B / (ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "config": {"workload": f"hidden [{B}, {D}] x weight [{C}, {D}]^T -> FW loss, "
+                                                        f"{C // world} classes per GPU", "form": impl,
+                                            "forward_gemm_tflop": 2.0 * B * D * C / 1e12},
+        }), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
 def main():
     a = parse()
     if a.impl == "reference":
@@ -664,6 +725,8 @@ def main():
     if a.mode == "class-sharded":
         return run_class_sharded(a)
     if a.mode == "lm-head":
+        if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+            return run_lm_head_vocab_parallel(a)
         return run_lm_head(a)
     return run_ours(a)
 

@@ -518,7 +518,37 @@ int fw_weight_grad_keys(const int32_t* sup_cols, int S, const int32_t* kappa, co
   const int64_t blocks = (n + threads - 1) / threads;
   return launch_status(launch(fw_weight_keys_kernel, dim3((unsigned)(blocks < 65535 ? blocks : 65535)),
                               dim3(threads), 1, static_cast<cudaStream_t>(stream), sup_cols, S, kappa, y, B, C,
-                              keys));
+                              keys, (int64_t)0));
+}
+
+int fw_weight_grad_keys_shard(const int32_t* sup_cols, int S, const int32_t* kappa, const int64_t* y, int64_t B,
+                              int64_t c0, int64_t C_shard, int64_t* keys, void* stream) {
+  if (B < 0 || S < 1 || C_shard < 1 || c0 < 0) return FWB_E_SHAPE;
+  if (B == 0) return FWB_OK;
+  if (!sup_cols || !kappa || !y || !keys) return FWB_E_POINTER;
+  const int64_t n = B * (int64_t)(S + 1);
+  const int threads = 256;
+  const int64_t blocks = (n + threads - 1) / threads;
+  return launch_status(launch(fw_weight_keys_kernel, dim3((unsigned)(blocks < 65535 ? blocks : 65535)),
+                              dim3(threads), 1, static_cast<cudaStream_t>(stream), sup_cols, S, kappa, y, B, C_shard,
+                              keys, c0));
+}
+
+int fw_sparse_grad_hidden_shard(int dtype, const void* weight_shard, int64_t c0, int64_t C_shard, int64_t D,
+                                const int32_t* sup_cols, int S, const int32_t* kappa, const int64_t* y, int64_t B,
+                                float scale, const float* grad_output, int per_row, float* dhidden_part,
+                                void* stream) {
+  if (dtype != FWB_DTYPE_F32 && dtype != FWB_DTYPE_BF16) return FWB_E_DTYPE;
+  if (B < 0 || C_shard < 1 || D < 1 || S < 1 || c0 < 0) return FWB_E_SHAPE;
+  if (B == 0) return FWB_OK;
+  if (!weight_shard || !sup_cols || !kappa || !y || !grad_output || !dhidden_part) return FWB_E_POINTER;
+  SparseGradArgs a = {weight_shard, dhidden_part, B, C_shard, D, sup_cols, S, kappa, y, scale, grad_output, per_row,
+                      c0};
+  const dim3 grid(aux_grid(B, 1)), block(kSparseThreads);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return launch_status(dtype == FWB_DTYPE_BF16
+                           ? launch(fw_sparse_dhidden_kernel<__nv_bfloat16, float>, grid, block, 1, st, a)
+                           : launch(fw_sparse_dhidden_kernel<float, float>, grid, block, 1, st, a));
 }
 
 int fw_segment_grad_weight(int dtype, const void* hidden, int64_t B, int64_t D, const int64_t* keys, int64_t nkeys,

@@ -160,19 +160,24 @@ struct SparseGradArgs {
   float scale;
   const float* go;       // upstream gradient (device)
   int per_row;
+  int64_t c0;            // sup_cols and y are global class ids; src/dst rows of the
+                         // weight cover classes [c0, c0 + C) (0 for a whole weight)
 };
 
 constexpr int kSparseThreads = 256;
 constexpr int kSparseCols = 8;  // D columns per thread per pass
 
 // dhidden[r] = go * scale * (sum_j W[j] / kappa - W[y]); one CTA per row.
-template <class T>
+// Only the classes j in [c0, c0 + C) held by W contribute (all of them for a
+// whole weight); a vocabulary-parallel rank writes its partial sum in fp32
+// (TO = float) for the all-reduce.
+template <class T, class TO = T>
 __global__ void __launch_bounds__(kSparseThreads) fw_sparse_dhidden_kernel(SparseGradArgs a) {
   const T* W = static_cast<const T*>(a.src);
-  T* dH = static_cast<T*>(a.dst);
+  TO* dH = static_cast<TO*>(a.dst);
   for (int64_t r = blockIdx.x; r < a.B; r += gridDim.x) {
     const int kap = a.kappa[r];
-    const int64_t yl = a.y[r];
+    const int64_t yl = a.y[r] - a.c0;
     const bool yok = yl >= 0 && yl < a.C;
     const float g = a.go[a.per_row ? r : 0] * a.scale;
     const float inv = kap > 0 ? (float)((double)g / (double)kap) : 0.0f;
@@ -182,7 +187,9 @@ __global__ void __launch_bounds__(kSparseThreads) fw_sparse_dhidden_kernel(Spars
 #pragma unroll
       for (int i = 0; i < kSparseCols; ++i) acc[i] = 0.0f;
       for (int k = 0; k < kap; ++k) {
-        const T* wr = W + (int64_t)cols[k] * a.D;
+        const int64_t j = (int64_t)cols[k] - a.c0;
+        if (j < 0 || j >= a.C) continue;  // a class held by another rank
+        const T* wr = W + j * a.D;
 #pragma unroll
         for (int i = 0; i < kSparseCols; ++i) {
           const int64_t d = d0 + (int64_t)i * kSparseThreads + threadIdx.x;
@@ -239,8 +246,11 @@ __global__ void __launch_bounds__(kSparseThreads) fw_sparse_dweight_kernel(Spars
 // Columns without contributions are left to the caller (zero).
 constexpr int64_t kNoKey = 0x7fffffffffffffffLL;
 
+// Keys of the classes in [c0, c0 + C) only, with class ids relative to c0
+// (c0 = 0 and C = all classes for a whole weight).
 __global__ void fw_weight_keys_kernel(const int32_t* __restrict__ sup_cols, int S, const int32_t* __restrict__ kappa,
-                                      const int64_t* __restrict__ y, int64_t B, int64_t C, int64_t* __restrict__ keys) {
+                                      const int64_t* __restrict__ y, int64_t B, int64_t C, int64_t* __restrict__ keys,
+                                      int64_t c0) {
   const int64_t n = B * (int64_t)(S + 1);
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = e / (S + 1);
@@ -249,9 +259,10 @@ __global__ void fw_weight_keys_kernel(const int32_t* __restrict__ sup_cols, int 
     int64_t key = kNoKey;
     if (kap > 0) {
       if (k < kap) {
-        key = ((int64_t)sup_cols[r * S + k] << 32) | (r << 1);
+        const int64_t j = (int64_t)sup_cols[r * S + k] - c0;
+        if (j >= 0 && j < C) key = (j << 32) | (r << 1);
       } else if (k == S) {
-        const int64_t yl = y[r];
+        const int64_t yl = y[r] - c0;
         if (yl >= 0 && yl < C) key = (yl << 32) | (r << 1) | 1;
       }
     }

@@ -471,6 +471,42 @@ torch::Tensor weight_grad_keys(torch::Tensor sup_cols, torch::Tensor kappa, torc
   return keys;
 }
 
+// Vocabulary-parallel rank: fp32 partial dhidden [B, D] from the local weight
+// shard (classes [c0, c0 + C_shard)).
+torch::Tensor sparse_grad_hidden_shard(torch::Tensor weight_shard, int64_t c0, torch::Tensor sup_cols,
+                                       torch::Tensor kappa, torch::Tensor targets, double scale,
+                                       torch::Tensor grad_output, bool per_row) {
+  TORCH_CHECK(weight_shard.is_cuda() && weight_shard.dim() == 2 && weight_shard.is_contiguous(),
+              "weight_shard must be contiguous [C_shard, D]");
+  TORCH_CHECK(sup_cols.scalar_type() == torch::kInt32 && sup_cols.is_contiguous() && sup_cols.dim() == 2,
+              "sup_cols must be contiguous int32 [B, S]");
+  const c10::cuda::CUDAGuard guard(weight_shard.device());
+  const int64_t B = kappa.numel();
+  auto dH = torch::empty({B, weight_shard.size(1)}, weight_shard.options().dtype(torch::kFloat32));
+  auto go = grad_output.to(weight_shard.device(), torch::kFloat32).contiguous();
+  check_rc(fw_sparse_grad_hidden_shard(lm_dtype(weight_shard), weight_shard.data_ptr(), c0, weight_shard.size(0),
+                                       weight_shard.size(1), sup_cols.data_ptr<int32_t>(), (int)sup_cols.size(1),
+                                       kappa.data_ptr<int32_t>(), targets.data_ptr<int64_t>(), B, (float)scale,
+                                       go.data_ptr<float>(), per_row ? 1 : 0, dH.data_ptr<float>(), cur_stream()),
+           "fw_sparse_grad_hidden_shard");
+  return dH;
+}
+
+torch::Tensor weight_grad_keys_shard(torch::Tensor sup_cols, torch::Tensor kappa, torch::Tensor targets, int64_t c0,
+                                     int64_t C_shard) {
+  TORCH_CHECK(sup_cols.is_cuda() && sup_cols.scalar_type() == torch::kInt32 && sup_cols.dim() == 2 &&
+                  sup_cols.is_contiguous(),
+              "sup_cols must be contiguous int32 [B, S]");
+  const c10::cuda::CUDAGuard guard(sup_cols.device());
+  const int64_t B = sup_cols.size(0), S = sup_cols.size(1);
+  auto keys = torch::empty({B * (S + 1)}, sup_cols.options().dtype(torch::kLong));
+  check_rc(fw_weight_grad_keys_shard(sup_cols.data_ptr<int32_t>(), (int)S, kappa.data_ptr<int32_t>(),
+                                     targets.data_ptr<int64_t>(), B, c0, C_shard, keys.data_ptr<int64_t>(),
+                                     cur_stream()),
+           "fw_weight_grad_keys_shard");
+  return keys;
+}
+
 void segment_grad_weight(torch::Tensor hidden, torch::Tensor sorted_keys, torch::Tensor kappa, double scale,
                          torch::Tensor grad_output, bool per_row, torch::Tensor dweight) {
   TORCH_CHECK(hidden.is_cuda() && hidden.dim() == 2 && hidden.is_contiguous(), "hidden must be contiguous [B, D]");
@@ -509,6 +545,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sparse_grad_hidden", &sparse_grad_hidden, "LM head backward: dhidden from the sparse logit gradient");
   m.def("sparse_grad_weight", &sparse_grad_weight, "LM head backward: dweight += (fp32 accumulator)");
   m.def("weight_grad_keys", &weight_grad_keys, "LM head backward: contribution keys [B * (S + 1)]");
+  m.def("sparse_grad_hidden_shard", &sparse_grad_hidden_shard,
+        "vocabulary-parallel LM head backward: this rank's fp32 part of dhidden");
+  m.def("weight_grad_keys_shard", &weight_grad_keys_shard,
+        "vocabulary-parallel LM head backward: contribution keys of the local classes");
   m.def("segment_grad_weight", &segment_grad_weight, "LM head backward: deterministic dweight rows from sorted keys");
   m.def("shard_solve", &shard_solve, "class-sharded step 3: global solve from gathered summaries",
         py::arg("gathered"), py::arg("rank"), py::arg("col_start"), py::arg("z_local"), py::arg("targets"),

@@ -53,6 +53,9 @@ _SIGS["fw_fused_fwd_bwd_f64"] = ([_P, _P, _I64, _I64, _I64, ctypes.c_double, _P,
                                  ctypes.c_int)
 _SIGS["fw_scale_grad_f64"] = ([_P, _P, ctypes.c_int, ctypes.c_double, _I64, _I64, _I64, _P], ctypes.c_int)
 _SIGS["fw_loss_reduce_f64"] = ([_P, _I64, ctypes.c_double, _P, _P], ctypes.c_int)
+_SIGS["fw_sparse_grad_hidden_shard"] = ([ctypes.c_int, _P, _I64, _I64, _I64, _P, ctypes.c_int, _P, _P, _I64,
+                                         ctypes.c_float, _P, ctypes.c_int, _P, _P], ctypes.c_int)
+_SIGS["fw_weight_grad_keys_shard"] = ([_P, ctypes.c_int, _P, _P, _I64, _I64, _I64, _P, _P], ctypes.c_int)
 _SIGS["fw_lmhead_fused_loss_noalloc"] = ([ctypes.c_int, _P, _I64, _I64, _P, _I64, ctypes.c_int, _P, ctypes.c_int,
                                           _P, _P, _P, _P, _P, _P, _P, _P, _P], ctypes.c_int)
 DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}

@@ -108,40 +108,53 @@ def _full_logits(hidden_rows, weight):
     return _logits_chunk(hidden_rows, weight)
 
 
+def chunk_summaries(hidden, weight, target, col_start, K, fused, c0=0):
+    """Per-(chunk, row) summary records of logits = hidden @ weight^T for the
+    column chunks col_start (offsets into weight's rows).  weight holds the
+    classes [c0, c0 + C) of the model (c0 = 0 for a whole weight); target
+    carries global class ids.  Returns (summaries [n, B, 4 + K],
+    local_idx [n, B, K], zy [B], status [1]) where zy[r] is the label logit
+    when the label lies in this weight's classes and 0 otherwise."""
+    fw = ext()
+    B = hidden.shape[0]
+    nchunks = len(col_start) - 1
+    dev = hidden.device
+    summaries = torch.empty((nchunks, B, 4 + K), dtype=torch.int32, device=dev)
+    local_idx = torch.empty((nchunks, B, K), dtype=torch.int32, device=dev)
+    zy = torch.zeros(B, dtype=torch.float32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    if fused:
+        y_local = target - c0 if c0 else target
+        fw.lmhead_fused_scan(hidden, weight, y_local, col_start, summaries, local_idx, zy, status)
+    else:
+        # The GEMM of chunk q+1 (tensor cores) runs while chunk q is being
+        # summarised on a second stream (HBM-bound); a chunk's memory is
+        # released only after its scan (record_stream).
+        main = torch.cuda.current_stream(dev)
+        side = _side_stream(dev)
+        side.wait_stream(main)
+        for q in range(nchunks):
+            q0, q1 = col_start[q], col_start[q + 1]
+            z = _logits_chunk(hidden, weight[q0:q1])
+            ready = torch.cuda.Event()
+            ready.record(main)
+            with torch.cuda.stream(side):
+                side.wait_event(ready)
+                fw.shard_scan_into(z, K, summaries[q], local_idx[q])
+                fw.label_logits(z, target, c0 + q0, zy)
+            z.record_stream(side)
+            del z
+        main.wait_stream(side)
+    return summaries, local_idx, zy, status
+
+
 class _FWLMHead(torch.autograd.Function):
     @staticmethod
     def forward(ctx, hidden, weight, target, scale, nchunks, K, fused):
         fw = ext()
-        B = hidden.shape[0]
         C = weight.shape[0]
         col_start = tile_col_start(C, nchunks) if fused else even_col_start(C, nchunks)
-        nchunks = len(col_start) - 1
-        dev = hidden.device
-        summaries = torch.empty((nchunks, B, 4 + K), dtype=torch.int32, device=dev)
-        local_idx = torch.empty((nchunks, B, K), dtype=torch.int32, device=dev)
-        zy = torch.empty(B, dtype=torch.float32, device=dev)
-        status = torch.zeros(1, dtype=torch.int32, device=dev)
-        if fused:
-            fw.lmhead_fused_scan(hidden, weight, target, col_start, summaries, local_idx, zy, status)
-        else:
-            # The GEMM of chunk q+1 (tensor cores) runs while chunk q is being
-            # summarised on a second stream (HBM-bound); a chunk's memory is
-            # released only after its scan (record_stream).
-            main = torch.cuda.current_stream(dev)
-            side = _side_stream(dev)
-            side.wait_stream(main)
-            for q in range(nchunks):
-                c0, c1 = col_start[q], col_start[q + 1]
-                z = _logits_chunk(hidden, weight[c0:c1])
-                ready = torch.cuda.Event()
-                ready.record(main)
-                with torch.cuda.stream(side):
-                    side.wait_event(ready)
-                    fw.shard_scan_into(z, K, summaries[q], local_idx[q])
-                    fw.label_logits(z, target, c0, zy)
-                z.record_stream(side)
-                del z
-            main.wait_stream(side)
+        summaries, local_idx, zy, status = chunk_summaries(hidden, weight, target, col_start, K, fused)
         H, kappa, loss_rows, sup_cols, fb_rows, fb_count = fw.chunks_solve(summaries, local_idx, col_start, zy, target)
         out = fw.loss_reduce(loss_rows, float(scale))
         # one read after the step's work is queued: exact-path row count and

@@ -281,6 +281,28 @@ FWB_API int fw_segment_grad_weight(int dtype, const void* hidden, int64_t B, int
                                    void* dweight, void* stream);
 
 /*
+ * Vocabulary-parallel LM head: rank q holds the weight rows of classes
+ * [c0, c0 + C_shard) and all ranks hold the same hidden, labels and (after
+ * an all-gather of the chunk summaries and fw_chunks_solve) the same support
+ * columns sup_cols (global class ids) and kappa.  No counterpart in the
+ * reference (its logits are whole); the math is the reference's
+ * (reference_impl.py:11-26).
+ *   fw_sparse_grad_hidden_shard: this rank's part of dhidden, in fp32 for the
+ *     all-reduce:  dhidden_part[r] = g_r (sum_{j in supp, j local} W[j - c0] /
+ *     kappa_r - [y_r local] W[y_r - c0]); rows with kappa 0 are written as 0.
+ *   fw_weight_grad_keys_shard: the keys of fw_weight_grad_keys restricted to
+ *     the local classes, with class ids relative to c0, for
+ *     fw_segment_grad_weight on the local weight gradient.
+ */
+FWB_API int fw_sparse_grad_hidden_shard(int dtype, const void* weight_shard, int64_t c0, int64_t C_shard,
+                                        int64_t D, const int32_t* sup_cols, int S, const int32_t* kappa,
+                                        const int64_t* y, int64_t B, float scale, const float* grad_output,
+                                        int per_row, float* dhidden_part, void* stream);
+
+FWB_API int fw_weight_grad_keys_shard(const int32_t* sup_cols, int S, const int32_t* kappa, const int64_t* y,
+                                      int64_t B, int64_t c0, int64_t C_shard, int64_t* keys, void* stream);
+
+/*
  * Deterministic (fixed-order, fp64) reduction out[0] = scale * sum_r loss[r].
  * Gives the "mean" (scale 1/B) and "sum" (scale 1) values of the reference
  * (reference_impl.py:28-31, src/cuda/fw_radix_argmax.cu:1411,1493,
