@@ -339,26 +339,38 @@ __global__ void __launch_bounds__(kST, 5)
     if (ovf) atomicOr(&s.flags, 1);
   }
   __syncthreads();
-  if (tid == 0) {
-    float cm = -CUDART_INF_F;
+  float M;
+  int row_flags;
+  if constexpr (CS == 1) {
+    // One CTA per row: every thread reads the warp maxima itself, so the
+    // row needs no second and third barrier.
+    M = -CUDART_INF_F;
 #pragma unroll
-    for (int k = 0; k < kSW; ++k) cm = max_nan(cm, s.wmax[k]);
-    s.cta_max = cm;
-  }
-  row_barrier<CS>();
-  if (tid == 0) {
-    float M = -CUDART_INF_F;
-    int flags = 0;
-    for (int r = 0; r < CS; ++r) {
-      const StreamShared* rs = cta_smem<CS>(&s, r);
-      M = max_nan(M, rs->cta_max);
-      flags |= rs->flags;
+    for (int k = 0; k < kSW; ++k) M = max_nan(M, s.wmax[k]);
+    row_flags = s.flags;
+  } else {
+    if (tid == 0) {
+      float cm = -CUDART_INF_F;
+#pragma unroll
+      for (int k = 0; k < kSW; ++k) cm = max_nan(cm, s.wmax[k]);
+      s.cta_max = cm;
     }
-    s.row_max = M;
-    s.row_flags = flags;
+    row_barrier<CS>();
+    if (tid == 0) {
+      float rm = -CUDART_INF_F;
+      int flags = 0;
+      for (int r = 0; r < CS; ++r) {
+        const StreamShared* rs = cta_smem<CS>(&s, r);
+        rm = max_nan(rm, rs->cta_max);
+        flags |= rs->flags;
+      }
+      s.row_max = rm;
+      s.row_flags = flags;
+    }
+    __syncthreads();
+    M = s.row_max;
+    row_flags = s.row_flags;
   }
-  __syncthreads();
-  const float M = s.row_max;
   const double Md = (double)M;
   const float t0 = __fsub_rd(M, 1.0f);
   const int64_t ylab = a.y ? a.y[row] : -1;  // no labels in kOutShard
@@ -414,7 +426,16 @@ __global__ void __launch_bounds__(kST, 5)
   }
 
   // ---------------------------------------------------------------- gather
-  if (!(s.row_flags & 1) && leader && w == 0) {
+  const bool lists_ok = !(row_flags & 1);  // no warp list overflowed
+  if constexpr (CS == 1) {
+    // One CTA: the warp lists hold at most kSW * kStreamListCap <= kSolveCap
+    // candidates, so the gathered list cannot overflow and warp 0 alone
+    // finishes the row; the zero stores of the other warps precede the
+    // barrier above, which orders them before warp 0's patch.
+    static_assert(kSW * kStreamListCap <= kSolveCap, "one CTA's lists must fit the solve list");
+    if (lists_ok && w != 0) return;
+  }
+  if (lists_ok && leader && w == 0) {
     int n = 0;
     bool full = false;
     for (int r = 0; r < CS && !full; ++r) {
@@ -449,8 +470,12 @@ __global__ void __launch_bounds__(kST, 5)
       for (int r = 0; r < CS; ++r) cta_smem<CS>(&s, r)->go_dense = full ? 1 : 0;
     }
   }
-  row_barrier<CS>();
-  const bool dense = (s.row_flags & 1) || s.go_dense;
+  if constexpr (CS == 1) {
+    __syncwarp();  // warp 0: the list and its size, written by the gather above
+  } else {
+    row_barrier<CS>();
+  }
+  const bool dense = (row_flags & 1) || s.go_dense;
 
   // ------------------------------------------------------ solve and patch
   if (!dense) {
