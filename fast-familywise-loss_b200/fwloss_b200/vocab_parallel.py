@@ -20,8 +20,8 @@ Per step, on every rank:
      kappa, the loss and the global support columns.  No logit crosses
      NVLink, only B * nchunks * (4 + 2K) int32 words per rank;
   4. backward: each rank's part of dhidden (its support columns and label
-     rows of W, fp32) is all-reduced; dweight is local (sorted contribution
-     keys of the local classes, deterministic).
+     rows of W, fp32) is all-reduced while dweight is computed; dweight is
+     local (sorted contribution keys of the local classes, deterministic).
 Rows whose chunk supports exceed K entries (near-constant logits) are solved
 from their full logit rows: each rank computes its columns of those rows,
 they are all-gathered, and the unsharded fused kernel runs on them.
@@ -155,10 +155,16 @@ class _VocabParallelLMHead(torch.autograd.Function):
     def backward(ctx, g):
         hidden, weight_shard, target, kappa, sup_cols = ctx.saved_tensors
         go = g.float().reshape(1)
-        dH, dW = backward_parts(hidden, weight_shard, ctx.c0, target, kappa, sup_cols, ctx.scale, go, ctx.rows,
-                                ctx.g_rows, need_dh=ctx.needs_input_grad[0], need_dw=ctx.needs_input_grad[1])
-        if dH is not None:
-            dist.all_reduce(dH, group=ctx.group)  # fp32 partial sums of every rank's classes
+        args = (hidden, weight_shard, ctx.c0, target, kappa, sup_cols, ctx.scale, go, ctx.rows, ctx.g_rows)
+        dH = dW = work = None
+        if ctx.needs_input_grad[0]:
+            dH, _ = backward_parts(*args, need_dh=True, need_dw=False)
+            # fp32 partial sums of every rank's classes, summed while dweight is computed
+            work = dist.all_reduce(dH, group=ctx.group, async_op=True)
+        if ctx.needs_input_grad[1]:
+            _, dW = backward_parts(*args, need_dh=False, need_dw=True)
+        if work is not None:
+            work.wait()
             dH = dH.to(hidden.dtype)
         return dH, dW, None, None, None, None, None, None, None
 
