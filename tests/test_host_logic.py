@@ -50,3 +50,34 @@ def test_cpu_tensors_are_rejected():
         familywise_loss(torch.randn(3, 4), torch.zeros(3, dtype=torch.long), reduction="max")
     with pytest.raises(ValueError):
         FWLoss(4, reduction="avg")
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8, 16])
+@pytest.mark.parametrize("fused", [True, False])
+@pytest.mark.parametrize("B,C", [(8192, 128256), (300, 20000), (64, 5000), (4096, 1000)])
+def test_vocab_parallel_chunk_lists(world, fused, B, C):
+    """The chunk list every rank derives for the vocabulary-parallel LM head:
+    the same number of chunks per rank (the all-gathers need equal shapes),
+    within the combined solve's limits, starting on 256-column tiles of each
+    rank's own weight rows (fused kernel), covering [0, C) in order."""
+    from fwloss_b200.lm_head import FUSED_TILE
+    from fwloss_b200.sharded import even_col_start
+    from fwloss_b200.vocab_parallel import (LIST_CAP, MAX_CHUNKS, chunks_per_rank, global_chunk_starts,
+                                            local_chunk_starts)
+
+    K = 16
+    if C // world < 1 or K * world > LIST_CAP:
+        pytest.skip("shape outside the supported range")
+    cs = even_col_start(C, world)
+    n = chunks_per_rank(world, B, cs, K, fused, 148)
+    assert 1 <= n and n * world <= MAX_CHUNKS and n * world * K <= LIST_CAP
+    for q in range(world):
+        loc = local_chunk_starts(cs[q + 1] - cs[q], n, fused)
+        assert len(loc) - 1 == n and loc[0] == 0 and loc[-1] == cs[q + 1] - cs[q]
+        assert all(b > a for a, b in zip(loc, loc[1:]))
+        if fused:
+            assert all(c % FUSED_TILE == 0 for c in loc[:-1])
+    g = global_chunk_starts(cs, n, fused)
+    assert len(g) == world * n + 1 and g[0] == 0 and g[-1] == C
+    assert all(b > a for a, b in zip(g, g[1:]))
+    assert set(cs[:-1]) <= set(g)
