@@ -142,6 +142,47 @@ __global__ void __launch_bounds__(kAuxThreads)
   }
 }
 
+// fw_scale_grad_kernel for a gradient whose support columns were listed by
+// the forward (sup_cols [B, sup_k], first slot -1 when not listed): a row
+// with a finite factor != 1, kappa <= sup_k and a list rewrites only its
+// kappa support entries and its label entry (kappa + 1 elements instead of
+// reading the row); other rows scale the whole row as fw_scale_grad_kernel
+// does.  One warp per row.
+template <class T>
+__global__ void __launch_bounds__(kAuxThreads)
+    fw_scale_grad_cols_kernel(T* __restrict__ grad, int64_t ld, const int32_t* __restrict__ sup_cols, int sup_k,
+                              const int32_t* __restrict__ kappa, const int64_t* __restrict__ y,
+                              const float* __restrict__ grad_output, int per_row, float assumed, int64_t B,
+                              int64_t C) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (kAuxThreads / 32);
+  for (int64_t r = (int64_t)blockIdx.x * (kAuxThreads / 32) + (threadIdx.x >> 5); r < B; r += warps) {
+    const float f = grad_output[per_row ? r : 0] / assumed;
+    if (f == 1.0f) continue;
+    T* gr = grad + r * ld;
+    const int kap = kappa[r];
+    const int32_t* sc = sup_cols + r * (int64_t)sup_k;
+    const bool listed = isfinite(f) && kap >= 1 && kap <= sup_k && sc[0] >= 0;
+    if (listed) {
+      const int64_t yl = y[r];
+      bool yin = false;
+      for (int k = lane; k < kap; k += 32) {
+        const int col = sc[k];
+        yin |= (col == yl);
+        st_elem(gr + col, ld_elem(gr + col) * f);
+      }
+      yin = __any_sync(kFull, yin);
+      if (lane == 0 && !yin && yl >= 0 && yl < C) st_elem(gr + yl, ld_elem(gr + yl) * f);
+    } else {
+      const bool dense = !isfinite(f);
+      for (int64_t c = lane; c < C; c += 32) {
+        const float g = ld_elem(gr + c);
+        if (dense || g != 0.f) st_elem(gr + c, g * f);
+      }
+    }
+  }
+}
+
 // out[0] = scale * sum(loss[0..B)) with fp64 accumulation in a fixed order,
 // by CL CTAs (one thread-block cluster when CL > 1): CTA r owns the r-th of
 // CL equal slices of the 16-byte groups of `loss`; thread t of a CTA sums

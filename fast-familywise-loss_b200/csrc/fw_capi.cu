@@ -158,11 +158,13 @@ cudaError_t dispatch_stream(const RowArgs& a, cudaStream_t st) {
 template <class T, int OUT>
 int run_rows(const RowArgs& a, cudaStream_t st, bool vec) {
   if (a.B == 0) return FWB_OK;
+  // the streaming tier lists the support columns under a runtime check
+  constexpr int OUT_STREAM = (OUT == kOutGradCols) ? kOutGrad : OUT;
   cudaError_t e;
   if (a.C <= kWarpTierMaxC)
     e = vec ? dispatch_warp<T, true, OUT>(a, st) : dispatch_warp<T, false, OUT>(a, st);
   else
-    e = vec ? dispatch_stream<T, true, OUT>(a, st) : dispatch_stream<T, false, OUT>(a, st);
+    e = vec ? dispatch_stream<T, true, OUT_STREAM>(a, st) : dispatch_stream<T, false, OUT_STREAM>(a, st);
   return launch_status(e);
 }
 
@@ -295,6 +297,50 @@ int fw_fused_fwd_bwd_typed(int dtype, const void* z, const int64_t* y, int64_t B
   if (dtype == FWB_DTYPE_BF16) return run_rows<__nv_bfloat16, kOutGrad>(a, st, vec);
   if (dtype == FWB_DTYPE_F16) return run_rows<__half, kOutGrad>(a, st, vec);
   return run_rows<float, kOutGrad>(a, st, vec);
+}
+
+int fw_fused_fwd_bwd_cols(int dtype, const void* z, const int64_t* y, int64_t B, int64_t C, int64_t ld,
+                          float grad_scale, void* grad, float* H, float* loss, int32_t* kappa,
+                          int32_t* sup_cols, int sup_k, int32_t* status, void* stream) {
+  if (dtype != FWB_DTYPE_F32 && dtype != FWB_DTYPE_BF16 && dtype != FWB_DTYPE_F16) return FWB_E_DTYPE;
+  if (int rc = check_shape(B, C, ld)) return rc;
+  if (sup_k < 1 || sup_k > 1024) return FWB_E_CAPACITY;
+  if (B > 0 && (!z || !y || !grad || !kappa || !sup_cols)) return FWB_E_POINTER;
+  RowArgs a = base_args(z, y, B, C, ld, H, loss, kappa, status);
+  a.scale = grad_scale;
+  a.grad = grad;
+  a.sup_cols = sup_cols;
+  a.sup_k = sup_k;
+  const int64_t eps = dtype == FWB_DTYPE_F32 ? 4 : 8;
+  const bool vec = aligned16(z) && aligned16(grad) && (ld % eps == 0);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == FWB_DTYPE_BF16) return run_rows<__nv_bfloat16, kOutGradCols>(a, st, vec);
+  if (dtype == FWB_DTYPE_F16) return run_rows<__half, kOutGradCols>(a, st, vec);
+  return run_rows<float, kOutGradCols>(a, st, vec);
+}
+
+int fw_scale_grad_cols(int dtype, void* grad, int64_t ld, const int32_t* sup_cols, int sup_k,
+                       const int32_t* kappa, const int64_t* y, const float* grad_output, int per_row,
+                       float assumed_scale, int64_t B, int64_t C, void* stream) {
+  if (dtype != FWB_DTYPE_F32 && dtype != FWB_DTYPE_BF16 && dtype != FWB_DTYPE_F16) return FWB_E_DTYPE;
+  if (int rc = check_shape(B, C, ld)) return rc;
+  if (sup_k < 1 || sup_k > 1024) return FWB_E_CAPACITY;
+  if (B == 0) return FWB_OK;
+  if (!grad || !sup_cols || !kappa || !y || !grad_output) return FWB_E_POINTER;
+  const int64_t blocks = (B + kAuxThreads / 32 - 1) / (kAuxThreads / 32);
+  const dim3 grid((unsigned)(blocks < 65535 ? blocks : 65535)), block(kAuxThreads);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (dtype == FWB_DTYPE_BF16)
+    e = launch(fw_scale_grad_cols_kernel<__nv_bfloat16>, grid, block, 1, st, static_cast<__nv_bfloat16*>(grad), ld,
+               sup_cols, sup_k, kappa, y, grad_output, per_row, assumed_scale, B, C);
+  else if (dtype == FWB_DTYPE_F16)
+    e = launch(fw_scale_grad_cols_kernel<__half>, grid, block, 1, st, static_cast<__half*>(grad), ld, sup_cols,
+               sup_k, kappa, y, grad_output, per_row, assumed_scale, B, C);
+  else
+    e = launch(fw_scale_grad_cols_kernel<float>, grid, block, 1, st, static_cast<float*>(grad), ld, sup_cols,
+               sup_k, kappa, y, grad_output, per_row, assumed_scale, B, C);
+  return launch_status(e);
 }
 
 int fw_forward_mask(const float* z, const int64_t* y, int64_t B, int64_t C, int64_t ld,

@@ -28,7 +28,10 @@ constexpr unsigned kFull = 0xffffffffu;
 // support as a (value, column) list.
 // kOutShard: one column shard of a class-sharded row (fw_shard.cuh): zero
 // gradient shard, plus a summary record of the shard's own solve.
-enum OutMode : int { kOutGrad = 0, kOutMask = 1, kOutCand = 2, kOutShard = 3 };
+// kOutGradCols: kOutGrad that also lists the support columns (RowArgs::sup_cols);
+// a separate instance in the register tier so that kOutGrad carries no extra
+// code, a runtime check of sup_cols in the streaming tier.
+enum OutMode : int { kOutGrad = 0, kOutMask = 1, kOutCand = 2, kOutShard = 3, kOutGradCols = 4 };
 
 // Summary record of one row of one class shard (int32 words):
 //   [0] local maximum M_r (float bits)   [1] local support size kappa_r
@@ -133,6 +136,9 @@ struct RowArgs {
   int32_t* shard_sum;    // kOutShard: [B, kShardHeader + shard_k]
   int32_t* shard_idx;    // kOutShard: [B, shard_k]
   int shard_k;           // kOutShard: support entries kept per row
+  int32_t* sup_cols;     // kOutGrad, optional: [B, sup_k] support columns (the first
+                         // min(kappa, sup_k)); -1 in the first slot when not listed
+  int sup_k;
 };
 
 // max() that returns NaN when either input is NaN (fmaxf would drop it).

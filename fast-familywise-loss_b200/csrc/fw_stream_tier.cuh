@@ -399,6 +399,7 @@ __global__ void __launch_bounds__(kST, 5)
     if (OUT == kOutGrad) {
       st_elem(gr + j, a.scale - ((j == yc) ? a.scale : 0.0f));
       if (yok && j != yc) st_elem(gr + yc, -a.scale);
+      if (a.sup_cols) a.sup_cols[row * (int64_t)a.sup_k] = j;
     } else if (OUT == kOutMask) {
       mr[j] = 1;
     } else if (OUT == kOutCand) {
@@ -501,6 +502,18 @@ __global__ void __launch_bounds__(kST, 5)
       }
       ysel = __any_sync(kFull, ysel);
       if (lane == 0 && yok && !ysel) st_elem(gr + yc, -a.scale);
+      if (a.sup_cols) {  // the support's columns (first sup_k of them)
+        int32_t* sc = a.sup_cols + row * (int64_t)a.sup_k;
+        int pos0 = 0;
+        for (int k0 = 0; k0 < n && pos0 < a.sup_k; k0 += 32) {
+          const int k = k0 + lane;
+          const bool sel = (k < n) && (s.sz[k] > Hf);
+          const unsigned b = __ballot_sync(kFull, sel);
+          const int pos = pos0 + __popc(b & lanemask_lt(lane));
+          if (sel && pos < a.sup_k) sc[pos] = s.si[k];
+          pos0 += __popc(b);
+        }
+      }
     } else if (OUT == kOutMask) {
       for (int k = lane; k < n; k += 32)
         if (s.sz[k] > Hf) mr[s.si[k]] = 1;
@@ -655,6 +668,8 @@ __global__ void __launch_bounds__(kST, 5)
       if (c == yc) gv -= a.scale;
       st_elem(gr + c, gv);
     });
+    // dense rows do not list their support (consumers fall back to the row)
+    if (a.sup_cols && leader && tid == 0) a.sup_cols[row * (int64_t)a.sup_k] = -1;
   } else if (OUT == kOutMask) {
     for_each_element<T, CS, VEC>(zr, C, rank, [&](float x, int c) { mr[c] = sel_of(x) ? 1 : 0; });
   } else if (OUT == kOutShard) {

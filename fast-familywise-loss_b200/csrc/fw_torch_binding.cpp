@@ -251,6 +251,60 @@ void scale_grad(torch::Tensor grad, torch::Tensor grad_output, bool per_row, dou
            "fw_scale_grad");
 }
 
+// fused_fwd_bwd (float32/bfloat16/float16 logits) that also lists every row's
+// support columns: (grad, H, losses, kappa, sup_cols [N, sup_k] int32).
+std::vector<torch::Tensor> fused_fwd_bwd_cols(torch::Tensor logits, torch::Tensor targets, double grad_scale,
+                                              int64_t sup_k, c10::optional<torch::Tensor> status) {
+  check_logits(logits, true);
+  TORCH_CHECK(logits.scalar_type() != torch::kFloat64, "fused_fwd_bwd_cols takes 32- and 16-bit logits");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  const int64_t N = logits.size(0), K = logits.size(1);
+  check_targets(targets, N, logits);
+  int64_t ld = K;
+  auto z = rows_view(logits, &ld);
+  auto y = targets.contiguous();
+  auto grad = (ld == K) ? torch::empty({N, K}, logits.options())
+                        : torch::empty_strided({N, K}, {ld, 1}, logits.options());
+  auto H = torch::empty({N}, logits.options().dtype(torch::kFloat32));
+  auto losses = torch::empty({N}, logits.options().dtype(torch::kFloat32));
+  auto kappa = torch::empty({N}, i32(logits));
+  auto cols = torch::empty({N, sup_k}, i32(logits));
+  int32_t* st = nullptr;
+  if (status.has_value()) {
+    TORCH_CHECK(status->is_cuda() && status->scalar_type() == torch::kInt32 && status->numel() >= 1,
+                "status must be an int32 CUDA tensor");
+    st = status->data_ptr<int32_t>();
+  }
+  check_rc(fw_fused_fwd_bwd_cols(dtype_code(z), z.data_ptr(), y.data_ptr<int64_t>(), N, K, ld, (float)grad_scale,
+                                 grad.data_ptr(), H.data_ptr<float>(), losses.data_ptr<float>(),
+                                 kappa.data_ptr<int32_t>(), cols.data_ptr<int32_t>(), (int)sup_k, st, cur_stream()),
+           "fw_fused_fwd_bwd_cols");
+  return {grad, H, losses, kappa, cols};
+}
+
+// scale_grad for a gradient from fused_fwd_bwd_cols: rows with a listed
+// support rewrite kappa + 1 entries only.
+void scale_grad_cols(torch::Tensor grad, torch::Tensor sup_cols, torch::Tensor kappa, torch::Tensor targets,
+                     torch::Tensor grad_output, bool per_row, double assumed_scale) {
+  TORCH_CHECK(grad.is_cuda() && grad.dim() == 2 && grad.stride(1) == 1 &&
+                  (grad.scalar_type() == torch::kFloat32 || grad.scalar_type() == torch::kBFloat16 ||
+                   grad.scalar_type() == torch::kHalf),
+              "grad must be a row-major float32/bfloat16/float16 CUDA matrix");
+  TORCH_CHECK(sup_cols.scalar_type() == torch::kInt32 && sup_cols.is_contiguous() && sup_cols.dim() == 2 &&
+                  sup_cols.size(0) == grad.size(0),
+              "sup_cols must be contiguous int32 [N, sup_k]");
+  const c10::cuda::CUDAGuard guard(grad.device());
+  const int64_t ld = grad.size(0) > 1 ? grad.stride(0) : grad.size(1);
+  auto go = grad_output.to(grad.device(), torch::kFloat32).contiguous();
+  TORCH_CHECK(go.numel() >= (per_row ? grad.size(0) : 1), "grad_output too small");
+  auto y = targets.contiguous();
+  check_rc(fw_scale_grad_cols(dtype_code(grad), grad.data_ptr(), ld, sup_cols.data_ptr<int32_t>(),
+                              (int)sup_cols.size(1), kappa.data_ptr<int32_t>(), y.data_ptr<int64_t>(),
+                              go.data_ptr<float>(), per_row ? 1 : 0, (float)assumed_scale, grad.size(0),
+                              grad.size(1), cur_stream()),
+           "fw_scale_grad_cols");
+}
+
 // scale * sum(losses), fixed-order fp64 reduction; 0-d, of the losses' dtype
 // (float32 or float64).
 torch::Tensor loss_reduce(torch::Tensor losses, double scale) {
@@ -532,6 +586,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fused_fwd_bwd", &fused_fwd_bwd, "fused forward+backward: (grad, H, losses, kappa)",
         py::arg("logits"), py::arg("targets"), py::arg("grad_scale"), py::arg("status") = py::none());
   m.def("scale_grad", &scale_grad, "in-place grad scaling by a device-side grad_output");
+  m.def("fused_fwd_bwd_cols", &fused_fwd_bwd_cols,
+        "fused forward+backward listing the support columns: (grad, H, losses, kappa, sup_cols)",
+        py::arg("logits"), py::arg("targets"), py::arg("grad_scale"), py::arg("sup_k"),
+        py::arg("status") = py::none());
+  m.def("scale_grad_cols", &scale_grad_cols, "in-place grad scaling touching only the listed support");
   m.def("loss_reduce", &loss_reduce, "deterministic scale * sum(losses)");
   m.def("shard_scan", &shard_scan, "class-sharded step 1: local solve, zero gradient shard, summaries");
   m.def("shard_scan_into", &shard_scan_into, "summaries of one logit chunk into given buffers");

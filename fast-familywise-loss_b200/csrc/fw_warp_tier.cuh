@@ -103,7 +103,7 @@ __device__ __forceinline__ void warp_tier_nonfinite(const RowArgs& a, int64_t ro
       if (c < C && (isn ? (x != x) : (x == m))) best = min(best, (unsigned)c);
     }
   const int jstar = (int)group_min<G>(best, gmask);
-  if (OUT == kOutGrad) {
+  if (OUT == kOutGrad || OUT == kOutGradCols) {
     T* gr = static_cast<T*>(a.grad) + row * a.ld;
 #pragma unroll
     for (int i = 0; i < NS; ++i) {
@@ -117,6 +117,7 @@ __device__ __forceinline__ void warp_tier_nonfinite(const RowArgs& a, int64_t ro
       __syncwarp(gmask);
       if (li == 0) st_elem(gr + yc, ((yc == jstar) ? a.scale : 0.0f) - a.scale);
     }
+    if (OUT == kOutGradCols && li == 0) a.sup_cols[row * (int64_t)a.sup_k] = jstar;
   } else if (OUT == kOutMask) {
     uint8_t* mr = a.mask + row * a.C;
 #pragma unroll
@@ -179,7 +180,8 @@ __global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS * El
   constexpr int NV = NS * EPS;          // register values per lane
   constexpr int RPW = 32 / G;           // rows per warp
   constexpr int CAPG = kWarpListCap / RPW;
-  static_assert(OUT == kOutGrad || sizeof(T) == 4, "mask/candidate/shard outputs are fp32-only");
+  static_assert(OUT == kOutGrad || OUT == kOutGradCols || sizeof(T) == 4,
+                "mask/candidate/shard outputs are fp32-only");
   __shared__ float s_list[kWarpTierWarps][kWarpListCap];
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
@@ -282,7 +284,7 @@ __global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS * El
     }
     const float Hf = threshold_fp32(m, tau);  // x > Hf <=> x in the support
 
-    if (OUT == kOutGrad) {
+    if (OUT == kOutGrad || OUT == kOutGradCols) {
       // Support entries first; the label entry is rewritten by lane 0 after a
       // group barrier (which orders the two stores to that address).
       const float inv = (float)((double)a.scale / (double)kap);
@@ -297,6 +299,23 @@ __global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS * El
       if (yok) {
         __syncwarp(gmask);
         if (li == 0) st_elem(gr + yc, ((zy > Hf) ? inv : 0.0f) - a.scale);
+      }
+      if constexpr (OUT == kOutGradCols) {  // the support's columns, in lane order (first sup_k)
+        int cnt = 0;
+#pragma unroll
+        for (int s = 0; s < NV; ++s) cnt += (v[s] > Hf) ? 1 : 0;
+        int off = group_excl_scan<G>(cnt, li, gmask);
+        int32_t* sc = a.sup_cols + row * (int64_t)a.sup_k;
+        if (cnt > 0 && off < a.sup_k) {
+#pragma unroll
+          for (int i = 0; i < NS; ++i)
+#pragma unroll
+            for (int j = 0; j < EPS; ++j)
+              if (v[EPS * i + j] > Hf) {
+                if (off < a.sup_k) sc[off] = group_slot_col<G, EPS, VEC>(i, j, li);
+                ++off;
+              }
+        }
       }
     } else if (OUT == kOutMask) {
       uint8_t* mr = a.mask + row * a.C;

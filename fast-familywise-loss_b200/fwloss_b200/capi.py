@@ -34,6 +34,10 @@ _SIGS = {
     "fw_scale_grad_typed": ([ctypes.c_int, _P, _P, ctypes.c_int, ctypes.c_float, _I64, _I64, _I64, _P],
                             ctypes.c_int),
 }
+_SIGS["fw_fused_fwd_bwd_cols"] = ([ctypes.c_int, _P, _P, _I64, _I64, _I64, ctypes.c_float, _P, _P, _P, _P, _P,
+                                   ctypes.c_int, _P, _P], ctypes.c_int)
+_SIGS["fw_scale_grad_cols"] = ([ctypes.c_int, _P, _I64, _P, ctypes.c_int, _P, _P, _P, ctypes.c_int, ctypes.c_float,
+                                _I64, _I64, _P], ctypes.c_int)
 _SIGS["fw_shard_scan"] = ([_P, _I64, _I64, _I64, ctypes.c_int, _P, _P, _P, _P], ctypes.c_int)
 _SIGS["fw_shard_solve"] = ([_P, ctypes.c_int, ctypes.c_int, _P, _I64, ctypes.c_int, _P, _I64, _P,
                            ctypes.c_float, _P, _P, _P, _P, _P, _P, _P, _P, _P], ctypes.c_int)

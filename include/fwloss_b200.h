@@ -96,6 +96,33 @@ FWB_API int fw_fused_fwd_bwd_typed(int dtype, const void* z, const int64_t* y, i
                                    void* stream);
 
 /*
+ * fw_fused_fwd_bwd_typed that also lists each row's support columns:
+ * sup_cols[r * sup_k + p] for p < min(kappa[r], sup_k) (order unspecified);
+ * rows whose support is not listed (dense rows solved by the radix passes)
+ * get -1 in their first slot.  kappa is required.  1 <= sup_k <= 1024.  With
+ * fw_scale_grad_cols this gives the per-row ("none") reduction a backward
+ * that touches kappa + 1 entries per row instead of the whole row.
+ * Extends the forward of the CPU autograd function (src/cpu/fw_cpu.cpp:
+ * 722-733), which keeps the dense gradient for its backward.
+ */
+FWB_API int fw_fused_fwd_bwd_cols(int dtype, const void* z, const int64_t* y, int64_t B, int64_t C,
+                                  int64_t ld, float grad_scale, void* grad, float* H, float* loss,
+                                  int32_t* kappa, int32_t* sup_cols, int sup_k, int32_t* status,
+                                  void* stream);
+
+/*
+ * fw_scale_grad_typed for a gradient written by fw_fused_fwd_bwd_cols: row r
+ * is multiplied by grad_output[per_row ? r : 0] / assumed_scale; a row with a
+ * finite factor != 1 and a listed support of kappa <= sup_k entries rewrites
+ * only those entries and its label entry, other rows are handled as by
+ * fw_scale_grad_typed.  Replaces the scaling of the CPU autograd backward
+ * (src/cpu/fw_cpu.cpp:734-740).
+ */
+FWB_API int fw_scale_grad_cols(int dtype, void* grad, int64_t ld, const int32_t* sup_cols, int sup_k,
+                               const int32_t* kappa, const int64_t* y, const float* grad_output,
+                               int per_row, float assumed_scale, int64_t B, int64_t C, void* stream);
+
+/*
  * Forward producing the boolean support mask (uint8, [B, C] contiguous):
  * mask[r, j] = 1[z_rj > h*_r].  Replaces fw_radix_forward_small
  * (src/cuda/fw_radix_argmax.cu:1381-1414; binding.cpp:5,11); the reference

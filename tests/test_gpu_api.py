@@ -131,3 +131,62 @@ def test_status_word_and_rows():
     assert st.item() & 1
     assert torch.isnan(losses[0]) and torch.isfinite(losses[1:]).all()
     assert ext().version() == "0.1.0"
+
+
+LISTED = ["gauss_C37", "gauss_C1000", "gauss_mid_C3000", "gauss_mid_C32000", "ties_C128", "ties_C5000",
+          "dense_s1e-3_C1000", "dense_s1e-3_C40000", "twolevel_C700", "exact_ties", "neginf_C12000"]
+
+
+@pytest.mark.parametrize("name", LISTED)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_listed_support_forward_and_sparse_backward(name, dtype):
+    """fw_fused_fwd_bwd_cols writes what fw_fused_fwd_bwd writes (bit-exact)
+    and lists each row's support columns (or -1 for rows it does not list);
+    fw_scale_grad_cols then scales rows by per-row factors touching only the
+    listed entries, and must equal the scaled oracle gradient (factors 1,
+    non-finite and ordinary mixed)."""
+    gens = dict(cases.parity_cases())
+    zn, yn = gens[name]()
+    zt = torch.from_numpy(zn).to(dtype)
+    zn = zt.float().numpy()
+    B = len(yn)
+    z, y = zt.cuda(), torch.from_numpy(yn).cuda()
+    K = 8
+    ref = O.solve(zn, yn, 1.0)
+    g0, H0, l0, k0 = ext().fused_fwd_bwd(z, y, 1.0, None)
+    g, H, l, k, cols = ext().fused_fwd_bwd_cols(z, y, 1.0, K, None)
+    torch.cuda.synchronize()
+    assert torch.equal(g, g0) and torch.equal(H, H0) and torch.equal(l, l0) and torch.equal(k, k0)
+    kk, cc = k.cpu().numpy(), cols.cpu().numpy()
+    for r in range(B):
+        if cc[r, 0] < 0:
+            continue
+        want = np.nonzero(ref["mask"][r])[0]
+        n = min(kk[r], K)
+        if kk[r] <= K:
+            assert sorted(cc[r, :n].tolist()) == sorted(want.tolist()), (name, r)
+        else:
+            assert set(cc[r, :n].tolist()) <= set(want.tolist()), (name, r)
+    rng = np.random.default_rng(B)
+    f = rng.uniform(0.25, 3.0, B).astype(np.float32)
+    f[::5] = 1.0
+    go = torch.from_numpy(f).cuda()
+    ext().scale_grad_cols(g, cols, k, y, go, True, 1.0)
+    rtol = RTOL if dtype == torch.float32 else 2.0 ** -7
+    np.testing.assert_allclose(g.float().cpu().numpy(), ref["grad"] * f[:, None], rtol=rtol, atol=ATOL)
+
+
+def test_none_reduction_uses_the_listed_support():
+    """familywise_loss(reduction="none") on the streaming tier: per-row
+    weights (zero weights included) give the oracle gradient times the
+    weights."""
+    zn, yn = cases.gauss(40, 32000, 1.0, seed=3)()
+    B = len(yn)
+    ref = O.solve(zn, yn, 1.0)
+    z = torch.from_numpy(zn).cuda().requires_grad_(True)
+    y = torch.from_numpy(yn).cuda()
+    out = familywise_loss(z, y, reduction="none")
+    w = torch.linspace(0.0, 2.0, B, device="cuda")
+    w[7] = 1.0
+    (out * w).sum().backward()
+    np.testing.assert_allclose(z.grad.cpu().numpy(), ref["grad"] * w.cpu().numpy()[:, None], rtol=RTOL, atol=ATOL)
