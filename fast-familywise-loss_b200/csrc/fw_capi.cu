@@ -12,6 +12,7 @@
 // run with coalesced 32-bit accesses.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <climits>
 #include <cstdint>
 
@@ -31,15 +32,21 @@ namespace {
 constexpr int kMaxDevices = 64;
 constexpr int64_t kWarpTierMaxC = 2048;
 
+// Per-process caches below are filled on first use; concurrent callers may
+// both compute the same value, so they are atomics (relaxed: the values
+// never change once set).
 int sm_count() {
-  static int cache[kMaxDevices] = {0};
+  static std::atomic<int> cache[kMaxDevices] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 148;
-  if (dev < kMaxDevices && cache[dev] > 0) return cache[dev];
+  if (dev < kMaxDevices) {
+    const int c = cache[dev].load(std::memory_order_relaxed);
+    if (c > 0) return c;
+  }
   int n = 0;
   if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
     n = 148;
-  if (dev < kMaxDevices) cache[dev] = n;
+  if (dev < kMaxDevices) cache[dev].store(n, std::memory_order_relaxed);
   return n;
 }
 
@@ -99,13 +106,14 @@ cudaError_t launch_warp_tier(const RowArgs& a, cudaStream_t st) {
   const bool fullv = VEC && (a.C % Elem<T>::kEPS == 0);
   auto k = fullv ? fw_warp_rows_kernel<T, G, NS, VEC, OUT, VEC>
                  : fw_warp_rows_kernel<T, G, NS, VEC, OUT, false>;
-  static int occ[2] = {0, 0};  // resident CTAs per SM of the two instances
-  int& o = occ[fullv ? 1 : 0];
+  static std::atomic<int> occ[2] = {};  // resident CTAs per SM of the two instances
+  int o = occ[fullv ? 1 : 0].load(std::memory_order_relaxed);
   if (o == 0) {
     int r = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, k, kWarpTierThreads, 0) != cudaSuccess || r < 1)
       r = 1;
     o = r;
+    occ[fullv ? 1 : 0].store(o, std::memory_order_relaxed);
   }
   const int64_t rows_per_block = (int64_t)kWarpTierWarps * (32 / G);
   const int64_t need = (a.B + rows_per_block - 1) / rows_per_block;
@@ -197,11 +205,13 @@ RowArgs base_args(const void* z, const int64_t* y, int64_t B, int64_t C, int64_t
 template <int TW, bool VEC>
 cudaError_t launch_f64(const F64Args& a, cudaStream_t st) {
   auto k = fw_f64_rows_kernel<TW, VEC>;
-  static int occ = 0;
+  static std::atomic<int> occ_cache{0};
+  int occ = occ_cache.load(std::memory_order_relaxed);
   if (occ == 0) {
     int r = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, k, kF64Threads, 0) != cudaSuccess || r < 1) r = 1;
     occ = r;
+    occ_cache.store(occ, std::memory_order_relaxed);
   }
   constexpr int64_t rows_per_block = kF64Warps / TW;
   const int64_t need = (a.B + rows_per_block - 1) / rows_per_block;
@@ -650,14 +660,14 @@ int fw_lmhead_fused_scan(int dtype, const void* hidden, int64_t B, int64_t D, co
   CUtensorMap tm_h, tm_w;
   if (!make_tile_map_bf16(&tm_h, hidden, B, D, kTcBM) || !make_tile_map_bf16(&tm_w, weight, C, D, kTcBN))
     return FWB_E_LAUNCH;
-  static bool attr_set[kMaxDevices] = {false};
+  static std::atomic<bool> attr_set[kMaxDevices] = {};
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return FWB_E_LAUNCH;
-  if (dev < kMaxDevices && !attr_set[dev]) {
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return FWB_E_LAUNCH;
+  if (dev >= kMaxDevices || !attr_set[dev].load(std::memory_order_acquire)) {
     if (cudaFuncSetAttribute(fw_lmhead_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)kTcSmemBytes) != cudaSuccess)
       return FWB_E_LAUNCH;
-    attr_set[dev] = true;
+    if (dev < kMaxDevices) attr_set[dev].store(true, std::memory_order_release);
   }
   const int64_t nwork = (int64_t)a.n_mblocks * nchunks;
   const int64_t sms = sm_count();
