@@ -55,8 +55,11 @@ def parse():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
-    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--config", default="cfg2")
+    p.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-cuda"],
+                   help="reference: the reference's CPU implementation (the reference arm); reference-cuda: "
+                        "the reference's own CUDA extension built for sm_100a, timed on the GPU beside ours")
+    p.add_argument("--config", default="cfg2",
+                   help="cfg0..cfg4, or gaussBxC (N(0,1) logits, the reference CUDA benchmark's workload)")
     p.add_argument("--e2e-steps", type=int, default=0, help="0: min(steps, 10)")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -81,7 +84,7 @@ def workload_desc(name, B, C, world, esize=4):
              "cfg3": "8 levels + 1% signed zeros", "cfg4": "N(0,1) +8 at a non-label class"}
     return {
         "workload": f"{name}: FWLoss fwd+bwd, B={B} x C={C}, {dict([(8, 'fp64'), (4, 'fp32'), (2, '16-bit')])[esize]} "
-                    f"logits {kinds.get(name, '')}, int64 labels",
+                    f"logits {kinds.get(name, 'N(0,1)' if name.startswith('gauss') else '')}, int64 labels",
         "rows_per_gpu": B, "classes": C, "global_batch": B * world,
         "parallelism": f"row-sharded dp{world}" + (" + scalar NCCL all-reduce" if world > 1 else ""),
         "l2": f"inputs {B * C * esize / 1e6:.1f} MB logits + {B * C * esize / 1e6:.1f} MB gradient per step"
@@ -218,7 +221,7 @@ def run_reference(a):
     import torch
     from fwloss_b200 import workloads
 
-    B, C = workloads.CONFIGS[a.config]
+    B, C = workloads.shape_of(a.config)
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     from oracle import ref_cpu
@@ -258,6 +261,54 @@ def run_reference(a):
     return 0
 
 
+def run_reference_cuda(a):
+    """The reference's own CUDA path (src/cuda/fw_radix_argmax.cu, built for
+    sm_100a by oracle/build.py) on the same workload, one GPU, inputs
+    resident in HBM, dispatched as its benchmark does
+    (CE_FW_perf.py:76-88); CUDA events over exactly K steps.  Prints a line
+    with impl "reference-cuda" (rank 0 only)."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    import torch
+
+    from fwloss_b200 import workloads
+    from oracle import ref_cuda
+
+    if not ref_cuda.available():
+        print(json.dumps({"impl": "reference-cuda", "unavailable": "reference CUDA extension not built "
+                                                                    "(oracle/build.py needs the reference checkout)"}))
+        return 0
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, C = workloads.shape_of(a.config)
+    z_cpu, y_cpu = workloads.make(a.config)
+    copies = 1 if B * C * 4 > 3 * L2_BYTES else min(64, -(-3 * L2_BYTES // (B * C * 4)))
+    zs = [z_cpu.to(dev) for _ in range(copies)]
+    y = y_cpu.to(dev)
+    for i in range(max(3, a.warmup)):
+        ref_cuda.forward_backward(zs[i % copies], y)
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(a.steps):
+        ref_cuda.forward_backward(zs[i % copies], y)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / a.steps
+    alg = B * (8 * C + 12)
+    peak, peak_kind = measured_peak()
+    print(json.dumps({
+        "impl": "reference-cuda", "metric": METRIC, "value": B / (ms / 1e3), "unit": UNIT, "n_gpus": 1,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_desc(a.config, B, C, 1),
+        "path": "fw_forward_small + fw_backward_small" if C < 10000 else "fw_forward + fw_backward",
+        "hbm": {"alg_bytes_per_step": alg, "achieved_gbs": alg / (ms / 1e3) / 1e9,
+                "frac": alg / (ms / 1e3) / 1e9 / peak, "peak": peak, "peak_kind": peak_kind},
+    }), flush=True)
+    return 0
+
+
 def run_ours(a):
     import torch
     import torch.distributed as dist
@@ -274,7 +325,7 @@ def run_ours(a):
     dev = torch.device("cuda", local)
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    B, C = workloads.CONFIGS[a.config]
+    B, C = workloads.shape_of(a.config)
     fw = ext()
 
     # inputs: rank 0 gets the configuration itself, other ranks the same recipe
@@ -722,6 +773,8 @@ def main():
     a = parse()
     if a.impl == "reference":
         return run_reference(a)
+    if a.impl == "reference-cuda":
+        return run_reference_cuda(a)
     if a.mode == "class-sharded":
         return run_class_sharded(a)
     if a.mode == "lm-head":

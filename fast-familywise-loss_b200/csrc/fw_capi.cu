@@ -137,9 +137,9 @@ cudaError_t dispatch_warp(const RowArgs& a, cudaStream_t st) {
 }
 
 // ----------------------------------------------------------- stream tier
-template <class T, int CS, bool VEC, int OUT>
+template <class T, int CS, bool VEC, int OUT, bool DEEP = false>
 cudaError_t launch_stream_tier(const RowArgs& a, cudaStream_t st) {
-  auto k = fw_stream_rows_kernel<T, CS, VEC, OUT>;
+  auto k = fw_stream_rows_kernel<T, CS, VEC, OUT, DEEP>;
   const int64_t grid = a.B * CS;
   return launch(k, dim3((unsigned)grid), dim3(kST), CS, st, a);
 }
@@ -156,7 +156,9 @@ int choose_cluster(int64_t B, int64_t C) {
 template <class T, bool VEC, int OUT>
 cudaError_t dispatch_stream(const RowArgs& a, cudaStream_t st) {
   switch (choose_cluster(a.B, a.C)) {
-    case 8: return launch_stream_tier<T, 8, VEC, OUT>(a, st);
+    case 8:  // at most two CTAs per SM: the instance with deeper load pipelining
+      return (a.B * 8 <= 2 * (int64_t)sm_count()) ? launch_stream_tier<T, 8, VEC, OUT, true>(a, st)
+                                                  : launch_stream_tier<T, 8, VEC, OUT>(a, st);
     case 4: return launch_stream_tier<T, 4, VEC, OUT>(a, st);
     case 2: return launch_stream_tier<T, 2, VEC, OUT>(a, st);
     default: return launch_stream_tier<T, 1, VEC, OUT>(a, st);

@@ -58,9 +58,22 @@ constexpr int kStreamScalars = 16;    // scalar loads per thread per streaming s
 
 // Loads per thread per streaming step: four 16-byte loads in flight for every
 // element type (16 fp32 or 32 bf16/fp16 values), 16 scalars without VEC.
-template <bool VEC>
+// DEEP instances (a grid of at most two CTAs per SM: very few rows, each on a
+// cluster of 8 CTAs) keep eight 16-byte loads in flight per thread instead,
+// since few CTAs share an SM (B200, B = 32 x C = 1e6 fp32: 93.2 -> 83.1 us).
+template <bool VEC, bool DEEP = false>
 __host__ __device__ constexpr int stream_ipt() {
-  return VEC ? kStreamItems : kStreamScalars;
+  return VEC ? (DEEP ? 2 * kStreamItems : kStreamItems) : kStreamScalars;
+}
+
+// Resident CTAs per SM the register budget is sized for: five (<= 51
+// registers; 16-bit rows stream in half the time of fp32 ones, so more CTAs
+// are needed to cover each row's exchange/solve/patch phase: B200, cfg2
+// shape, bf16 99.1 -> 97.0 us, fp32 unchanged, six CTAs slower); two for the
+// DEEP instances, whose threads hold twice the values.
+template <bool DEEP>
+__host__ __device__ constexpr int stream_min_blocks() {
+  return DEEP ? 2 : 5;
 }
 
 struct __align__(16) StreamShared {
@@ -217,12 +230,8 @@ __device__ __forceinline__ void for_each_element(const T* zr, int64_t C,
   }
 }
 
-// Five resident CTAs per SM (<= 51 registers): 16-bit rows stream in half
-// the time of fp32 ones, so more CTAs are needed to cover each row's
-// exchange/solve/patch phase (B200, cfg2 shape: bf16 99.1 -> 97.0 us, fp32
-// unchanged; six CTAs were slower).
-template <class T, int CS, bool VEC, int OUT>
-__global__ void __launch_bounds__(kST, 5)
+template <class T, int CS, bool VEC, int OUT, bool DEEP = false>
+__global__ void __launch_bounds__(kST, stream_min_blocks<DEEP>())
     fw_stream_rows_kernel(RowArgs a) {
   allow_dependent_launch();
   static_assert(OUT == kOutGrad || sizeof(T) == 4, "mask/candidate/shard outputs are fp32-only");
@@ -250,7 +259,7 @@ __global__ void __launch_bounds__(kST, 5)
 
   // ---------------------------------------------------------------- stream
   constexpr int W = VEC ? EPS : 1;
-  constexpr int IPT = stream_ipt<VEC>();
+  constexpr int IPT = stream_ipt<VEC, DEEP>();
   const Segment g = row_segment<CS, VEC, EPS>(C, rank);
   float run = -CUDART_INF_F;
   int wcnt = 0;

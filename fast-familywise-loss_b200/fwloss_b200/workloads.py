@@ -79,10 +79,35 @@ def _cfg4_block(block, rows, C):
     return z, y
 
 
+def shape_of(name):
+    """(B, C) of a configuration name: cfg0..cfg4 or 'gaussBxC'."""
+    return parse_gaussian(name) or CONFIGS[name]
+
+
+def make_gaussian(B, C, sigma=1.0, seed=0):
+    """N(0, sigma^2) logits [B, C] and uniform labels: the reference's CUDA
+    benchmark workload (benchmarks/cuda_benchmarks/CE_FW_perf.py, B = 32)."""
+    g = _gen(seed)
+    z = torch.randn(B, C, generator=g) * float(sigma)
+    y = torch.randint(0, C, (B,), generator=g)
+    return z, y
+
+
+def parse_gaussian(name):
+    """'gaussBxC' -> (B, C), else None (bench configurations of that form)."""
+    if not name.startswith("gauss"):
+        return None
+    B, C = name[5:].split("x")
+    return int(B), int(C)
+
+
 def make_rank(name, rank):
     """The batch of one rank under weak scaling: rank 0 gets the configuration
     itself, rank r > 0 the same recipe with its own rows (cfg4: row blocks
     r*B.. of the block-seeded stream; others: seed + 7919 r)."""
+    shape = parse_gaussian(name)
+    if shape:
+        return make_gaussian(*shape, seed=rank)
     if rank == 0:
         return make(name)
     B, C = CONFIGS[name]
@@ -98,6 +123,9 @@ def make(name, rows=None, cols=None):
     `rows`/`cols` shrink the configuration (same recipe and seed, fewer rows or
     classes); for cfg4, `rows` selects the first row blocks and a partial last
     block (each block from its own seed)."""
+    shape = parse_gaussian(name)
+    if shape:
+        return make_gaussian(shape[0] if rows is None else int(rows), shape[1] if cols is None else int(cols))
     B, C = CONFIGS[name]
     B = B if rows is None else int(rows)
     C = C if cols is None else int(cols)

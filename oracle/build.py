@@ -13,6 +13,15 @@
                                      (src/cpu/fwcpp.py:12-16): -O3 -fopenmp
                                      -fno-math-errno.
 
+  oracle/_ref/fw_radix_cuda_ref*.so  the reference's own CUDA extension
+                                     (src/cuda/fw_radix_argmax.cu and
+                                     src/cuda/binding.cpp, the two sources its
+                                     setup.py:7-13 builds), compiled for
+                                     sm_100a where they lie, as module
+                                     fw_radix_cuda_ref: the GPU baseline that
+                                     the benchmark times next to ours and a
+                                     parity check of kappa.
+
 The reference build needs the checkout (FW_REF_PATH, default
 /root/reference); where it is absent (e.g. on a GPU box) the prebuilt files
 travel with the tree and this step is skipped.
@@ -80,9 +89,57 @@ def build_ref(force=False):
     return out
 
 
+REF_CUDA_SRCS = [os.path.join(REF_PATH, "src", "cuda", f) for f in ("fw_radix_argmax.cu", "binding.cpp")]
+
+
+def ref_cuda_module_path():
+    return os.path.join(REF_OUT, f"fw_radix_cuda_ref{SUFFIX}")
+
+
+def build_ref_cuda(force=False):
+    """nvcc / g++ on the reference's two CUDA-extension sources, with the
+    defines torch's CUDAExtension passes (the reference's setup.py adds no
+    flags of its own), for sm_100a."""
+    if not all(os.path.exists(p) for p in REF_CUDA_SRCS):
+        return None
+    target = ref_cuda_module_path()
+    if not force and not _stale(target, REF_CUDA_SRCS):
+        return target
+    import torch
+    from torch.utils import cpp_extension as ce
+
+    os.makedirs(REF_OUT, exist_ok=True)
+    os.makedirs(BUILD, exist_ok=True)
+    incs = ce.include_paths(device_type="cuda") + [sysconfig.get_paths()["include"]]
+    libdirs = ce.library_paths(device_type="cuda")
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    defs = ["-DTORCH_EXTENSION_NAME=fw_radix_cuda_ref", "-DTORCH_API_INCLUDE_EXTENSION_H",
+            f"-D_GLIBCXX_USE_CXX11_ABI={abi}"]
+    cuda_home = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    nvcc = os.path.join(cuda_home, "bin", "nvcc")
+    cu_obj = os.path.join(BUILD, "fw_radix_argmax_ref.o")
+    cpp_obj = os.path.join(BUILD, "binding_ref.o")
+    cmd = [nvcc, "-c", REF_CUDA_SRCS[0], "-o", cu_obj, "-gencode", "arch=compute_100a,code=sm_100a", "-O3",
+           "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr", "-D__CUDA_NO_HALF_OPERATORS__",
+           "-D__CUDA_NO_HALF_CONVERSIONS__", "-D__CUDA_NO_BFLOAT16_CONVERSIONS__",
+           "-D__CUDA_NO_HALF2_OPERATORS__", "-w"] + defs + [f"-I{p}" for p in incs]
+    subprocess.run(cmd, check=True)
+    cmd = ["g++", "-c", REF_CUDA_SRCS[1], "-o", cpp_obj, "-O2", "-std=c++17", "-fPIC",
+           "-Wno-deprecated-declarations"] + defs + [f"-I{p}" for p in incs + [os.path.join(cuda_home, "include")]]
+    subprocess.run(cmd, check=True)
+    cmd = ["g++", "-shared", cu_obj, cpp_obj, "-o", target + ".tmp"]
+    cmd += [f"-L{p}" for p in libdirs + [os.path.join(cuda_home, "lib64")]]
+    cmd += [f"-Wl,-rpath,{p}" for p in libdirs]
+    cmd += ["-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-ltorch_python", "-lcudart"]
+    subprocess.run(cmd, check=True)
+    os.replace(target + ".tmp", target)
+    return target
+
+
 def build(force=False):
     build_oracle(force)
     build_ref(force)
+    build_ref_cuda(force)
 
 
 if __name__ == "__main__":
@@ -90,3 +147,4 @@ if __name__ == "__main__":
     print(ORACLE_SO)
     for isa in ISAS:
         print(ref_module_path(isa), os.path.exists(ref_module_path(isa)))
+    print(ref_cuda_module_path(), os.path.exists(ref_cuda_module_path()))
