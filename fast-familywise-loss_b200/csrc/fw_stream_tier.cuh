@@ -85,6 +85,8 @@ struct __align__(16) StreamShared {
   int hc[256];
   float wmax[kSW];
   int wcnt[kSW];
+  int gcnt[8 * kSW];  // cluster gather: kept candidates per (rank, warp) list
+  int goff[8 * kSW];  // and their offsets in the solve list
   unsigned run_key;
   int flags;        // bit 0: a warp list overflowed
   float cta_max;
@@ -365,16 +367,20 @@ __global__ void __launch_bounds__(kST, stream_min_blocks<DEEP>())
       s.cta_max = cm;
     }
     row_barrier<CS>();
-    if (tid == 0) {
+    if (w == 0) {  // one remote read per lane instead of CS serial ones
       float rm = -CUDART_INF_F;
       int flags = 0;
-      for (int r = 0; r < CS; ++r) {
-        const StreamShared* rs = cta_smem<CS>(&s, r);
-        rm = max_nan(rm, rs->cta_max);
-        flags |= rs->flags;
+      if (lane < CS) {
+        const StreamShared* rs = cta_smem<CS>(&s, lane);
+        rm = rs->cta_max;
+        flags = rs->flags;
       }
-      s.row_max = rm;
-      s.row_flags = flags;
+      rm = warp_max_nan(rm);
+      flags = (int)__reduce_or_sync(kFull, (unsigned)flags);
+      if (lane == 0) {
+        s.row_max = rm;
+        s.row_flags = flags;
+      }
     }
     __syncthreads();
     M = s.row_max;
@@ -445,7 +451,68 @@ __global__ void __launch_bounds__(kST, stream_min_blocks<DEEP>())
     static_assert(kSW * kStreamListCap <= kSolveCap, "one CTA's lists must fit the solve list");
     if (lists_ok && w != 0) return;
   }
-  if (lists_ok && leader && w == 0) {
+  if constexpr (CS > 1) {
+    // The leader CTA's warps gather the CS * kSW lists in parallel (their
+    // entries sit in other CTAs' shared memory): kept counts per list, their
+    // offsets in the fixed list order (rank-major, then warp), then the
+    // copies.  Same list, in the same order, as one warp walking the lists.
+    if (lists_ok && leader) {
+      constexpr int NL = CS * kSW;
+      for (int L = w; L < NL; L += kSW) {
+        const StreamShared* rs = cta_smem<CS>(&s, L / kSW);
+        const int ww = L % kSW;
+        const int cnt = rs->wcnt[ww];
+        int kept = 0;
+        for (int k0 = 0; k0 < cnt; k0 += 32) {
+          const int k = k0 + lane;
+          kept += __popc(__ballot_sync(kFull, (k < cnt) && (rs->lz[ww][k] > t0)));
+        }
+        if (lane == 0) s.gcnt[L] = kept;
+      }
+      __syncthreads();
+      if (w == 0) {
+        int tot = 0;
+        for (int L0 = 0; L0 < NL; L0 += 32) {
+          const int L = L0 + lane;
+          const int c = (L < NL) ? s.gcnt[L] : 0;
+          const int x = warp_excl_scan(c, lane);
+          if (L < NL) s.goff[L] = tot + x;
+          tot += __reduce_add_sync(kFull, c);
+        }
+        if (lane == 0) {
+          const bool full = tot > kSolveCap;
+          s.nsolve = full ? 0 : tot;
+          for (int r = 0; r < CS; ++r) cta_smem<CS>(&s, r)->go_dense = full ? 1 : 0;
+        }
+      }
+      __syncthreads();
+      if (!s.go_dense) {
+        for (int L = w; L < NL; L += kSW) {
+          const StreamShared* rs = cta_smem<CS>(&s, L / kSW);
+          const int ww = L % kSW;
+          const int cnt = rs->wcnt[ww];
+          int pos0 = s.goff[L];
+          for (int k0 = 0; k0 < cnt; k0 += 32) {
+            const int k = k0 + lane;
+            float val = -CUDART_INF_F;
+            int col = 0;
+            if (k < cnt) {
+              val = rs->lz[ww][k];
+              col = rs->li[ww][k];
+            }
+            const bool keep = val > t0;
+            const unsigned b = __ballot_sync(kFull, keep);
+            if (keep) {
+              const int pos = pos0 + __popc(b & lanemask_lt(lane));
+              s.sz[pos] = val;
+              s.si[pos] = col;
+            }
+            pos0 += __popc(b);
+          }
+        }
+      }
+    }
+  } else if (lists_ok && w == 0) {
     int n = 0;
     bool full = false;
     for (int r = 0; r < CS && !full; ++r) {
