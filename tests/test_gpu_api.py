@@ -190,3 +190,35 @@ def test_none_reduction_uses_the_listed_support():
     w[7] = 1.0
     (out * w).sum().backward()
     np.testing.assert_allclose(z.grad.cpu().numpy(), ref["grad"] * w.cpu().numpy()[:, None], rtol=RTOL, atol=ATOL)
+
+
+@pytest.mark.parametrize("C", [1000, 32000])
+def test_forward_backward_captured_in_a_cuda_graph(C):
+    """familywise_loss forward + backward never synchronises with the host
+    and allocates fixed shapes, so a training step can be captured once in a
+    CUDA graph and replayed on new logits copied into the same buffer."""
+    B = 64
+    z = torch.zeros(B, C, device="cuda", requires_grad=True)
+    y = torch.zeros(B, dtype=torch.int64, device="cuda")
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            z.grad = None
+            familywise_loss(z, y, reduction="mean").backward()
+    torch.cuda.current_stream().wait_stream(side)
+    z.grad = None
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        loss = familywise_loss(z, y, reduction="mean")
+        loss.backward()
+    for seed in (1, 2):
+        zn, yn = cases.gauss(B, C, 1.0, seed=seed)()
+        with torch.no_grad():
+            z.copy_(torch.from_numpy(zn))
+        y.copy_(torch.from_numpy(yn))
+        graph.replay()
+        torch.cuda.synchronize()
+        ref = O.solve(zn, yn, 1.0 / B)
+        np.testing.assert_allclose(loss.item(), ref["loss"].mean(), rtol=RTOL, atol=ATOL)
+        np.testing.assert_allclose(z.grad.cpu().numpy(), ref["grad"], rtol=RTOL, atol=ATOL)
