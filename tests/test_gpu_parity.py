@@ -323,3 +323,35 @@ def test_half_precision_autograd(dtype):
     assert z.grad.dtype == tdt
     np.testing.assert_allclose(out.float().item(), ref["loss"].mean(), rtol=rtol)
     np.testing.assert_allclose(z.grad.float().cpu().numpy(), ref["grad"], rtol=rtol, atol=ATOL)
+
+
+# Batch sizes around the streaming tier's launch-shape switches on a 148-SM
+# B200: the cluster size (B * CS against 4 CTAs per SM), the deep-pipelining
+# instance (B * 8 <= 2 CTAs per SM) and the grid of one CTA per row.
+SHAPE_SWITCHES = [(1, 300000), (2, 65536), (37, 40000), (38, 40000), (73, 20000), (74, 20000),
+                  (147, 9000), (149, 9000), (295, 8200), (297, 8200), (600, 2049)]
+
+
+@pytest.mark.parametrize("B,C", SHAPE_SWITCHES, ids=[f"B{b}_C{c}" for b, c in SHAPE_SWITCHES])
+def test_streaming_launch_shape_switches(B, C):
+    """kappa bit-exact and H, loss, gradient within tolerance against the C
+    oracle on both sides of every launch-shape switch, with Gaussian rows
+    (a handful of candidates) and rows of near-ties (sigma 1e-3: the dense
+    radix path for half of them)."""
+    from oracle import ref_cpu
+
+    rng = np.random.default_rng(B * 1000 + C)
+    z = rng.standard_normal((B, C)).astype(np.float32)
+    z[1::2] *= np.float32(1e-3)
+    y = rng.integers(0, C, B).astype(np.int64)
+    tau, kap, M, loss = ref_cpu.c_solve(z, y)
+    out = _fused(z, y, 1.0 / B)
+    np.testing.assert_array_equal(out["kappa"], kap)
+    H = O.threshold_f32(tau, M)
+    np.testing.assert_allclose(out["H"], H, rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(out["loss"], loss, rtol=RTOL, atol=ATOL)
+    g = out["grad"]
+    sel = z > H[:, None]
+    expect = sel.astype(np.float64) / kap[:, None] / B
+    expect[np.arange(B), y] -= 1.0 / B
+    np.testing.assert_allclose(g, expect, rtol=RTOL, atol=ATOL)
