@@ -64,6 +64,9 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-graph", action="store_true", help="launch steps eagerly")
+    p.add_argument("--strong", action="store_true",
+                   help="rows mode: split the configuration's B rows across the ranks (strong scaling) instead "
+                        "of giving every rank B rows of its own (weak scaling, the default)")
     p.add_argument("--mode", default="rows", choices=["rows", "class-sharded", "lm-head"],
                    help="rows: rows sharded across GPUs (default); class-sharded: every GPU holds a "
                         "column shard of every row (vocabulary-parallel), cfg4 shape; lm-head: "
@@ -328,9 +331,22 @@ def run_ours(a):
     B, C = workloads.shape_of(a.config)
     fw = ext()
 
-    # inputs: rank 0 gets the configuration itself, other ranks the same recipe
-    # with their own seed (weak scaling: every rank owns B distinct rows)
-    z_cpu, y_cpu = workloads.make_rank(a.config, rank)
+    # inputs: weak scaling: rank 0 gets the configuration itself, other ranks
+    # the same recipe with their own seed (every rank owns B distinct rows);
+    # strong scaling: every rank takes its contiguous block of the
+    # configuration's B rows
+    if a.strong:
+        from fwloss_b200.distributed import shard_rows
+
+        Bg = B
+        lo, hi = shard_rows(B, rank, world)
+        z_all, y_all = workloads.make(a.config)
+        z_cpu, y_cpu = z_all[lo:hi].contiguous(), y_all[lo:hi].contiguous()
+        del z_all, y_all
+        B = hi - lo
+    else:
+        z_cpu, y_cpu = workloads.make_rank(a.config, rank)
+        Bg = B * world
     tdt = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16, "f64": torch.float64}[a.dtype]
     esize = torch.tensor([], dtype=tdt).element_size()
     z_cpu = z_cpu.to(tdt)
@@ -339,7 +355,6 @@ def run_ours(a):
     copies = 1 if B * C * esize > 3 * L2_BYTES else min(64, -(-3 * L2_BYTES // (B * C * esize)))
     zs = [z_cpu.to(dev) for _ in range(copies)]
     y = y_cpu.to(dev)
-    Bg = B * world
     scale = 1.0 / Bg
     stream = torch.cuda.current_stream(dev)
 
@@ -513,8 +528,9 @@ def run_ours(a):
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": ms / a.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": a.dtype, "data": "synthetic",
-            "config": dict(workload_desc(a.config, B, C, world, esize),
+            "scaling": "strong" if a.strong else "weak", "vs_baseline": None, "dtype": a.dtype,
+            "data": "synthetic",
+            "config": dict(workload_desc(a.config, B, C, world, esize), global_batch=Bg,
                            launch=("CUDA graph of the K timed steps" if use_graph and copies > 1 else
                                    "CUDA-graph replay of each step" if use_graph else "eager")),
             "hbm_gbs": alg_bytes * a.steps / (ms / 1e3) / 1e9,
