@@ -77,3 +77,34 @@ def test_dropin_module_surface():
         assert callable(getattr(fw_radix_cuda, fn))
     with pytest.raises(RuntimeError, match="CUDA"):
         fw_radix_cuda.fw_forward_small(torch.randn(2, 5), torch.zeros(2, dtype=torch.long))
+
+
+def test_argument_checks_of_the_later_entry_points():
+    """Shape, capacity, dtype and pointer checks that return before any device
+    work: the listed-support forms, the vocabulary-parallel backward and the
+    allocation-free LM-head forward."""
+    lib = capi.load()
+    P = None
+    d = ctypes.c_void_p(256)
+    # fw_fused_fwd_bwd_cols: dtype, shape, capacity (sup_k), pointers
+    assert lib.fw_fused_fwd_bwd_cols(9, d, d, 4, 10, 10, 1.0, d, P, P, d, d, 8, P, P) == 5
+    assert lib.fw_fused_fwd_bwd_cols(0, d, d, 4, 10, 9, 1.0, d, P, P, d, d, 8, P, P) == 1
+    assert lib.fw_fused_fwd_bwd_cols(0, d, d, 4, 10, 10, 1.0, d, P, P, d, d, 0, P, P) == 4
+    assert lib.fw_fused_fwd_bwd_cols(0, d, d, 4, 10, 10, 1.0, d, P, P, P, d, 8, P, P) == 2
+    assert lib.fw_fused_fwd_bwd_cols(0, d, d, 4, 10, 10, 1.0, d, P, P, d, P, 8, P, P) == 2
+    assert lib.fw_fused_fwd_bwd_cols(0, P, P, 0, 10, 10, 1.0, P, P, P, P, P, 8, P, P) == 0
+    # fw_scale_grad_cols
+    assert lib.fw_scale_grad_cols(0, d, 10, d, 0, d, d, d, 1, 1.0, 4, 10, P) == 4
+    assert lib.fw_scale_grad_cols(0, P, 10, d, 8, d, d, d, 1, 1.0, 4, 10, P) == 2
+    assert lib.fw_scale_grad_cols(0, d, 9, d, 8, d, d, d, 1, 1.0, 4, 10, P) == 1
+    # vocabulary-parallel backward
+    assert lib.fw_sparse_grad_hidden_shard(0, d, -1, 10, 8, d, 4, d, d, 4, 1.0, d, 0, d, P) == 1
+    assert lib.fw_sparse_grad_hidden_shard(2, d, 0, 10, 8, d, 4, d, d, 4, 1.0, d, 0, d, P) == 5
+    assert lib.fw_sparse_grad_hidden_shard(0, P, 0, 10, 8, d, 4, d, d, 4, 1.0, d, 0, d, P) == 2
+    assert lib.fw_weight_grad_keys_shard(d, 4, d, d, 4, 0, 0, d, P) == 1
+    assert lib.fw_weight_grad_keys_shard(P, 4, d, d, 4, 0, 10, d, P) == 2
+    # allocation-free LM-head forward: chunk count and workspace limits
+    cs = (ctypes.c_int64 * 3)(0, 256, 1000)
+    assert lib.fw_lmhead_fused_loss_noalloc(1, d, 4, 64, d, 1000, 0, cs, 8, d, P, d, P, d, d, d, P, P) == 4
+    assert lib.fw_lmhead_fused_loss_noalloc(1, d, 1 << 20, 64, d, 1000, 2, cs, 64, d, P, d, P, d, d, d, P, P) == 4
+    assert lib.fw_lmhead_fused_loss_noalloc(1, d, -1, 64, d, 1000, 2, cs, 8, d, P, d, P, d, d, d, P, P) == 1
