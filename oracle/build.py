@@ -22,9 +22,9 @@
                                      the benchmark times next to ours and a
                                      parity check of kappa.
 
-The reference build needs the checkout (FW_REF_PATH, default
-/root/reference); where it is absent (e.g. on a GPU box) the prebuilt files
-travel with the tree and this step is skipped.
+The reference build needs the reference checkout (environment variable
+FW_REF_PATH, or the default REF_PATH below); where it is absent (e.g. on a GPU
+box) the prebuilt files travel with the tree and this step is skipped.
 """
 import os
 import subprocess

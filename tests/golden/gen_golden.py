@@ -1,7 +1,8 @@
 """Writes the golden fixtures of tests/golden/ from the REFERENCE itself.
 
-Run in a container that has the reference checkout (FW_REF_PATH, default
-/root/reference) and the reference CPU extension built by oracle/build.py:
+Run in a container that has the reference checkout (environment variable
+FW_REF_PATH, or the default REF below) and the reference CPU extension built
+by oracle/build.py:
 
     python tests/golden/gen_golden.py
 
