@@ -113,7 +113,15 @@ def profile_traffic(name):
         return None
 
 
-class Clocks:
+def rows_traffic(t, rows, profiled_rows):
+    """The profiled launch's DRAM bytes scaled to a launch of `rows` rows (a
+    strong-scaling rank's share): the fused kernel's traffic is proportional
+    to the rows it processes."""
+    if t is None or rows == profiled_rows:
+        return t
+    f = rows / profiled_rows
+    return dict(t, bytes=int(t["bytes"] * f), dram_read=int(t["dram_read"] * f), dram_write=int(t["dram_write"] * f),
+                note=f"scaled from the profiled {profiled_rows}-row launch to this rank's {rows} rows")
     """nvidia-smi sampler (200 ms) around the timed region."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -537,7 +545,9 @@ def run_ours(a):
             "roofline": {"bound": "hbm", "kernel": ("fw_f64_rows_kernel" if esize == 8 else
                                                     "fw_stream_rows_kernel" if C > 2048 else "fw_warp_rows_kernel"),
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_kind": peak_kind, "traffic": profile_traffic(a.config if a.dtype == "f32" else f"{a.config}_{a.dtype}"),
+                         "peak_kind": peak_kind,
+                         "traffic": rows_traffic(profile_traffic(a.config if a.dtype == "f32" else
+                                                                 f"{a.config}_{a.dtype}"), B, Bg if a.strong else B),
                          "alg_bytes_per_launch": alg_bytes, "kernel_ms": k_ms},
             "cpu_baseline": cpu,
             "e2e": e2e,
