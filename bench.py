@@ -122,6 +122,9 @@ def rows_traffic(t, rows, profiled_rows):
     f = rows / profiled_rows
     return dict(t, bytes=int(t["bytes"] * f), dram_read=int(t["dram_read"] * f), dram_write=int(t["dram_write"] * f),
                 note=f"scaled from the profiled {profiled_rows}-row launch to this rank's {rows} rows")
+
+
+class Clocks:
     """nvidia-smi sampler (200 ms) around the timed region."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
