@@ -21,6 +21,7 @@ CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 PKG = os.path.join(HERE, "fwloss_b200")
 LIB = os.path.join(PKG, "libfwloss_b200.so")
+BUILD_DIR = os.path.join(HERE, "_build")  # object files (git-ignored)
 EXT = os.path.join(HERE, "fw_radix_cuda" + sysconfig.get_config_var("EXT_SUFFIX"))
 
 NVCC_ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -43,16 +44,34 @@ def _cuda_sources():
     return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cu", ".cuh")))
 
 
-def build_lib(force=False, verbose=False):
-    deps = _cuda_sources() + [os.path.join(INCLUDE, "fwloss_b200.h")]
-    if not force and not _stale(LIB, deps):
-        return LIB
+def _compile_one(src, obj, verbose):
     cmd = [_nvcc(), *NVCC_ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
-           "-Xcompiler", "-fvisibility=hidden", "-shared", "-o", LIB + ".tmp",
-           os.path.join(CSRC, "fw_capi.cu"), os.path.join(CSRC, "fw_noalloc.cu")]
+           "-Xcompiler", "-fvisibility=hidden", "-c", "-o", obj, src]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
-    subprocess.run(cmd, check=True)
+    return subprocess.run(cmd, capture_output=True, text=True)
+
+
+def build_lib(force=False, verbose=False):
+    """Every .cu file of csrc/ is one translation unit (compiled in parallel
+    into BUILD_DIR), linked into one shared library."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    headers = [p for p in _cuda_sources() if p.endswith(".cuh")] + [os.path.join(INCLUDE, "fwloss_b200.h")]
+    units = [p for p in _cuda_sources() if p.endswith(".cu")]
+    if not force and not _stale(LIB, headers + units):
+        return LIB
+    os.makedirs(BUILD_DIR, exist_ok=True)
+    objs = [os.path.join(BUILD_DIR, os.path.basename(u)[:-3] + ".o") for u in units]
+    todo = [(u, o) for u, o in zip(units, objs) if force or _stale(o, [u] + headers)]
+    with ThreadPoolExecutor(max_workers=max(1, min(len(todo), os.cpu_count() or 1))) as ex:
+        results = list(ex.map(lambda uo: (uo[0], _compile_one(uo[0], uo[1], verbose)), todo))
+    for u, r in results:
+        if verbose or r.returncode != 0:
+            sys.stderr.write(r.stdout + r.stderr)
+        if r.returncode != 0:
+            raise subprocess.CalledProcessError(r.returncode, f"nvcc {u}")
+    subprocess.run([_nvcc(), *NVCC_ARCH, "-shared", "-Xcompiler", "-fPIC", "-o", LIB + ".tmp", *objs], check=True)
     os.replace(LIB + ".tmp", LIB)
     return LIB
 

@@ -1,15 +1,7 @@
-// C ABI of libfwloss_b200.so: argument checks, tier selection and launches.
-// Declarations and semantics: include/fwloss_b200.h.
-//
-// Tier selection by class count C (the tile shape scales with C):
-//   C <= 2048          a group of 8/16/32 lanes per row, row in registers
-//                      (fw_warp_tier.cuh).
-//   C  > 2048          CTA per row (CS = 1) or a cluster of CS = 2/4/8 CTAs per
-//                      row when there are too few rows to fill the GPU
-//                      (fw_stream_tier.cuh).
-// 128-bit loads/stores are used when every row starts on a 16-byte boundary
-// (base pointers 16-byte aligned and ld % 4 == 0); otherwise the same kernels
-// run with coalesced 32-bit accesses.
+// C ABI of libfwloss_b200.so: argument checks and launches.
+// Declarations and semantics: include/fwloss_b200.h.  The fused row kernels
+// (tier selection by class count) are launched through run_rows, whose
+// instances live in the fw_rows_*.cu translation units (fw_rows.cuh).
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -22,37 +14,11 @@
 #include "fw_f64.cuh"
 #include "fw_lmhead.cuh"
 #include "fw_lmhead_tc.cuh"
+#include "fw_host.cuh"
 #include "fw_shard.cuh"
-#include "fw_stream_tier.cuh"
-#include "fw_warp_tier.cuh"
 
 namespace fwb200 {
 namespace {
-
-constexpr int kMaxDevices = 64;
-constexpr int64_t kWarpTierMaxC = 2048;
-
-// Per-process caches below are filled on first use; concurrent callers may
-// both compute the same value, so they are atomics (relaxed: the values
-// never change once set).
-int sm_count() {
-  static std::atomic<int> cache[kMaxDevices] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 148;
-  if (dev < kMaxDevices) {
-    const int c = cache[dev].load(std::memory_order_relaxed);
-    if (c > 0) return c;
-  }
-  int n = 0;
-  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
-    n = 148;
-  if (dev < kMaxDevices) cache[dev].store(n, std::memory_order_relaxed);
-  return n;
-}
-
-inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-
-int launch_status(cudaError_t e) { return e == cudaSuccess ? FWB_OK : FWB_E_LAUNCH; }
 
 // The loss reduction: one CTA, or one cluster of kReduceCluster CTAs above
 // kReduceClusterMinRows rows, launched as a programmatic dependent of the
@@ -76,106 +42,6 @@ cudaError_t launch_loss_reduce(const T* loss, int64_t B, double scale, T* out, c
   const int vec = aligned16(loss) ? 1 : 0;
   return cl ? cudaLaunchKernelEx(&cfg, fw_loss_reduce_kernel<T, kReduceCluster>, loss, B, scale, out, vec)
             : cudaLaunchKernelEx(&cfg, fw_loss_reduce_kernel<T, 1>, loss, B, scale, out, vec);
-}
-
-template <class... KArgs, class... Args>
-cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, int cluster,
-                   cudaStream_t stream, Args&&... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  if (cluster > 1) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = cluster;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-  }
-  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
-}
-
-// ------------------------------------------------------------- warp tier
-template <class T, int G, int NS, bool VEC, int OUT>
-cudaError_t launch_warp_tier(const RowArgs& a, cudaStream_t st) {
-  // FULLV: every 16-byte slot fully inside or outside the row (one predicate
-  // per slot); only meaningful for 16-byte accesses
-  const bool fullv = VEC && (a.C % Elem<T>::kEPS == 0);
-  auto k = fullv ? fw_warp_rows_kernel<T, G, NS, VEC, OUT, VEC>
-                 : fw_warp_rows_kernel<T, G, NS, VEC, OUT, false>;
-  static std::atomic<int> occ[2] = {};  // resident CTAs per SM of the two instances
-  int o = occ[fullv ? 1 : 0].load(std::memory_order_relaxed);
-  if (o == 0) {
-    int r = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, k, kWarpTierThreads, 0) != cudaSuccess || r < 1)
-      r = 1;
-    o = r;
-    occ[fullv ? 1 : 0].store(o, std::memory_order_relaxed);
-  }
-  const int64_t rows_per_block = (int64_t)kWarpTierWarps * (32 / G);
-  const int64_t need = (a.B + rows_per_block - 1) / rows_per_block;
-  const int64_t cap = (int64_t)sm_count() * o;
-  const int grid = (int)(need < cap ? need : cap);
-  return launch(k, dim3(grid), dim3(kWarpTierThreads), 1, st, a);
-}
-
-// Lanes per row G and register values per lane NV by class count:
-//   C <= 64: 8 x 8,  <= 128: 8 x 16,  <= 256: 16 x 16,  <= 512: 32 x 16,
-//   <= 1024: 32 x 32,  <= 2048: 32 x 64  (NS = NV / EPS 16-byte slots).
-template <class T, bool VEC, int OUT>
-cudaError_t dispatch_warp(const RowArgs& a, cudaStream_t st) {
-  constexpr int E = Elem<T>::kEPS;
-  if (a.C <= 64) return launch_warp_tier<T, 8, 8 / E, VEC, OUT>(a, st);
-  if (a.C <= 128) return launch_warp_tier<T, 8, 16 / E, VEC, OUT>(a, st);
-  if (a.C <= 256) return launch_warp_tier<T, 16, 16 / E, VEC, OUT>(a, st);
-  if (a.C <= 512) return launch_warp_tier<T, 32, 16 / E, VEC, OUT>(a, st);
-  if (a.C <= 1024) return launch_warp_tier<T, 32, 32 / E, VEC, OUT>(a, st);
-  return launch_warp_tier<T, 32, 64 / E, VEC, OUT>(a, st);
-}
-
-// ----------------------------------------------------------- stream tier
-template <class T, int CS, bool VEC, int OUT, bool DEEP = false>
-cudaError_t launch_stream_tier(const RowArgs& a, cudaStream_t st) {
-  auto k = fw_stream_rows_kernel<T, CS, VEC, OUT, DEEP>;
-  const int64_t grid = a.B * CS;
-  return launch(k, dim3((unsigned)grid), dim3(kST), CS, st, a);
-}
-
-// Cluster size: the smallest CS in {1, 2, 4, 8} giving at least 4 CTAs per SM,
-// while every CTA keeps a segment of at least 4096 columns.
-int choose_cluster(int64_t B, int64_t C) {
-  const int64_t want = (int64_t)sm_count() * 4;
-  int cs = 1;
-  while (cs < 8 && B * cs < want && C / (cs * 2) >= 4096) cs *= 2;
-  return cs;
-}
-
-template <class T, bool VEC, int OUT>
-cudaError_t dispatch_stream(const RowArgs& a, cudaStream_t st) {
-  switch (choose_cluster(a.B, a.C)) {
-    case 8:  // at most two CTAs per SM: the instance with deeper load pipelining
-      return (a.B * 8 <= 2 * (int64_t)sm_count()) ? launch_stream_tier<T, 8, VEC, OUT, true>(a, st)
-                                                  : launch_stream_tier<T, 8, VEC, OUT>(a, st);
-    case 4: return launch_stream_tier<T, 4, VEC, OUT>(a, st);
-    case 2: return launch_stream_tier<T, 2, VEC, OUT>(a, st);
-    default: return launch_stream_tier<T, 1, VEC, OUT>(a, st);
-  }
-}
-
-template <class T, int OUT>
-int run_rows(const RowArgs& a, cudaStream_t st, bool vec) {
-  if (a.B == 0) return FWB_OK;
-  // the streaming tier lists the support columns under a runtime check
-  constexpr int OUT_STREAM = (OUT == kOutGradCols) ? kOutGrad : OUT;
-  cudaError_t e;
-  if (a.C <= kWarpTierMaxC)
-    e = vec ? dispatch_warp<T, true, OUT>(a, st) : dispatch_warp<T, false, OUT>(a, st);
-  else
-    e = vec ? dispatch_stream<T, true, OUT_STREAM>(a, st) : dispatch_stream<T, false, OUT_STREAM>(a, st);
-  return launch_status(e);
 }
 
 int check_shape(int64_t B, int64_t C, int64_t ld) {
@@ -219,6 +85,17 @@ cudaError_t launch_f64(const F64Args& a, cudaStream_t st) {
   const int64_t need = (a.B + rows_per_block - 1) / rows_per_block;
   const int64_t cap = (int64_t)sm_count() * occ;
   return launch(k, dim3((unsigned)(need < cap ? need : cap)), dim3(kF64Threads), 1, st, a);
+}
+
+// fp64 rows of any length; a.grad may be null (forward only).
+int run_f64(const F64Args& a, cudaStream_t st) {
+  const bool vec = aligned16(a.z) && (a.grad == nullptr || aligned16(a.grad)) && (a.ld % 2 == 0);
+  cudaError_t e;
+  if (a.C <= kF64WarpRowMaxC)
+    e = vec ? launch_f64<1, true>(a, st) : launch_f64<1, false>(a, st);
+  else
+    e = vec ? launch_f64<kF64Warps, true>(a, st) : launch_f64<kF64Warps, false>(a, st);
+  return launch_status(e);
 }
 
 // cuTensorMapEncodeTiled, looked up through the runtime so that the library
@@ -694,14 +571,30 @@ int fw_fused_fwd_bwd_f64(const double* z, const int64_t* y, int64_t B, int64_t C
   if (B == 0) return FWB_OK;
   if (!z || !y || !grad) return FWB_E_POINTER;
   const F64Args a = {z, y, B, C, ld, grad_scale, grad, H, loss, kappa, status};
-  const bool vec = aligned16(z) && aligned16(grad) && (ld % 2 == 0);
+  return run_f64(a, static_cast<cudaStream_t>(stream));
+}
+
+int fw_forward_rows(int dtype, const void* z, const int64_t* y, int64_t B, int64_t C, int64_t ld,
+                    float* H, float* loss, int32_t* kappa, int32_t* status, void* stream) {
+  if (dtype != FWB_DTYPE_F32 && dtype != FWB_DTYPE_BF16 && dtype != FWB_DTYPE_F16) return FWB_E_DTYPE;
+  if (int rc = check_shape(B, C, ld)) return rc;
+  if (B > 0 && (!z || !y)) return FWB_E_POINTER;
+  const RowArgs a = base_args(z, y, B, C, ld, H, loss, kappa, status);
+  const int64_t eps = dtype == FWB_DTYPE_F32 ? 4 : 8;
+  const bool vec = aligned16(z) && (ld % eps == 0);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e;
-  if (C <= kF64WarpRowMaxC)
-    e = vec ? launch_f64<1, true>(a, st) : launch_f64<1, false>(a, st);
-  else
-    e = vec ? launch_f64<kF64Warps, true>(a, st) : launch_f64<kF64Warps, false>(a, st);
-  return launch_status(e);
+  if (dtype == FWB_DTYPE_BF16) return run_rows<__nv_bfloat16, kOutNone>(a, st, vec);
+  if (dtype == FWB_DTYPE_F16) return run_rows<__half, kOutNone>(a, st, vec);
+  return run_rows<float, kOutNone>(a, st, vec);
+}
+
+int fw_forward_rows_f64(const double* z, const int64_t* y, int64_t B, int64_t C, int64_t ld, double* H,
+                        double* loss, int32_t* kappa, int32_t* status, void* stream) {
+  if (int rc = check_shape(B, C, ld)) return rc;
+  if (B == 0) return FWB_OK;
+  if (!z || !y) return FWB_E_POINTER;
+  const F64Args a = {z, y, B, C, ld, 1.0, nullptr, H, loss, kappa, status};
+  return run_f64(a, static_cast<cudaStream_t>(stream));
 }
 
 int fw_scale_grad_f64(double* grad, const double* grad_output, int per_row, double assumed_scale,

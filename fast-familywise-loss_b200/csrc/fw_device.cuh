@@ -31,7 +31,9 @@ constexpr unsigned kFull = 0xffffffffu;
 // kOutGradCols: kOutGrad that also lists the support columns (RowArgs::sup_cols);
 // a separate instance in the register tier so that kOutGrad carries no extra
 // code, a runtime check of sup_cols in the streaming tier.
-enum OutMode : int { kOutGrad = 0, kOutMask = 1, kOutCand = 2, kOutShard = 3, kOutGradCols = 4 };
+// kOutNone: forward only -- H, loss and kappa, no per-element output (the
+// logits are read once and nothing of size C is written).
+enum OutMode : int { kOutGrad = 0, kOutMask = 1, kOutCand = 2, kOutShard = 3, kOutGradCols = 4, kOutNone = 5 };
 
 // Summary record of one row of one class shard (int32 words):
 //   [0] local maximum M_r (float bits)   [1] local support size kappa_r

@@ -31,7 +31,9 @@
 //
 // Every mbarrier wait is bounded: on a timeout the kernel sets status bit
 // FWB_STATUS_TIMEOUT and a CTA-wide abort flag, every role leaves its loop,
-// and TMEM is released before the CTA exits.
+// the producer waits (bounded) for the TMA loads it issued to land, the MMA
+// warp commits to a drain barrier and waits (bounded) for its issued MMAs,
+// and only then is TMEM released and the CTA allowed to exit.
 #pragma once
 
 #include <cuda.h>
@@ -59,6 +61,7 @@ constexpr uint32_t kTcSmemBytes =
     1024 + kTcStages * (kTcABytes + kTcBBytes) + kTcListBytes + 256;
 constexpr int kTcStatusTimeout = 4;
 constexpr uint64_t kTcWaitLimitNs = 2000000000ull;  // 2 s; a tile's MMAs take ~20 us
+constexpr uint64_t kTcDrainLimitNs = 100000000ull;  // 100 ms per drain wait after an abort
 
 struct TcArgs {
   int64_t B;
@@ -133,6 +136,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     *abort_flag = 1;
   }
   return ok;
+}
+
+// Abort path, one thread: waits (at most kTcDrainLimitNs) for the phase of
+// the given parity to complete, i.e. for the asynchronous operations that
+// arrive on `bar` to finish writing.  Gives up silently at the limit.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try(bar, parity)) return;
+    if ((i & 255u) == 255u && global_ns() - t0 > kTcDrainLimitNs) return;
+  }
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
@@ -330,7 +344,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* empty = bars + kTcStages;        // [kTcStages] MMA -> TMA
   uint64_t* tfull = bars + 2 * kTcStages;    // [2] MMA -> epilogue
   uint64_t* tempty = tfull + 2;              // [2] epilogue -> MMA
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* drain = tempty + 2;              // abort path: completion of every issued MMA
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -344,6 +359,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&tfull[i], 1);
       mbar_init(&tempty[i], 4 * 32);
     }
+    mbar_init(drain, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -360,6 +376,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   const int64_t nwork = (int64_t)a.n_mblocks * a.nchunks;
   const int nk = (int)((a.D + kTcBK - 1) / kTcBK);
+  // Work still in flight when a role aborts: bit s of `issued` is set once
+  // stage s has had a TMA load issued, bit s of `issued_par` is the parity of
+  // that stage's last load; `mma_any` is set once an MMA has been issued.
+  uint32_t issued = 0u, issued_par = 0u;
+  bool mma_any = false;
 
   if (warp == 0) {
     // ------------------------------------------- TMA producer (lane 0 issues)
@@ -375,6 +396,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tma_load_2d(smA + s * kTcABytes, &tm_hidden, kb * kTcBK, m0, &full[s]);
             tma_load_2d(smB + s * kTcBBytes, &tm_weight, kb * kTcBK, (int)n0, &full[s]);
           }
+          issued |= 1u << s;
+          issued_par = (issued_par & ~(1u << s)) | (ph << s);
           __syncwarp();
           if (++s == kTcStages) {
             s = 0;
@@ -404,6 +427,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         (kb | k) != 0 ? 1u : 0u);
             umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
           }
+          mma_any = true;
           __syncwarp();
           if (++s == kTcStages) {
             s = 0;
@@ -456,6 +480,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   }
 done:
+  __syncwarp();
+  if (*abort_flag && lane == 0) {
+    // Aborted: let the copies and MMAs already issued land before the CTA
+    // frees its TMEM and shared memory (each wait bounded, kTcDrainLimitNs).
+    if (warp == 0) {
+      for (int st = 0; st < kTcStages; ++st)
+        if (issued & (1u << st)) mbar_drain(&full[st], (issued_par >> st) & 1u);
+    } else if (warp == 1 && mma_any) {
+      umma_commit(drain);  // arrives once every MMA issued by this thread is complete
+      mbar_drain(drain, 0u);
+    }
+  }
   __syncwarp();
   tc_fence_before();
   __syncthreads();

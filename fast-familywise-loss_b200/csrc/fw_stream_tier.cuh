@@ -236,7 +236,8 @@ template <class T, int CS, bool VEC, int OUT, bool DEEP = false>
 __global__ void __launch_bounds__(kST, stream_min_blocks<DEEP>())
     fw_stream_rows_kernel(RowArgs a) {
   allow_dependent_launch();
-  static_assert(OUT == kOutGrad || sizeof(T) == 4, "mask/candidate/shard outputs are fp32-only");
+  static_assert(OUT == kOutGrad || OUT == kOutNone || sizeof(T) == 4,
+                "mask/candidate/shard outputs are fp32-only");
   constexpr bool kZeroFill = (OUT == kOutGrad || OUT == kOutShard);
   constexpr int EPS = Elem<T>::kEPS;
   __shared__ StreamShared s;
@@ -421,6 +422,8 @@ __global__ void __launch_bounds__(kST, stream_min_blocks<DEEP>())
       a.cand_val[row * C] = ld_elem(zr + j);
       a.cand_idx[row * C] = j;
       if (a.cand_count) a.cand_count[row] = 1;
+    } else if (OUT == kOutNone) {
+      // forward only: no per-element output
     } else {  // kOutShard: the gradient shard stays zero
       int32_t* rec = a.shard_sum + row * (int64_t)(kShardHeader + a.shard_k);
       rec[0] = __float_as_int(M);
@@ -616,6 +619,8 @@ __global__ void __launch_bounds__(kST, stream_min_blocks<DEEP>())
         rec[3] = -1;
       }
       return;
+    } else if (OUT == kOutNone) {
+      // forward only: H, loss and kappa below
     } else {
       float* cv = a.cand_val + row * C;
       int32_t* ci = a.cand_idx + row * C;
@@ -770,6 +775,8 @@ __global__ void __launch_bounds__(kST, stream_min_blocks<DEEP>())
       rec[3] = -1;
     }
     return;
+  } else if (OUT == kOutNone) {
+    // forward only: the decision is all that is needed, no second pass
   } else {
     int* pos_ctr = &cta_smem<CS>(&s, 0)->cand_pos;
     float* cv = a.cand_val + row * C;

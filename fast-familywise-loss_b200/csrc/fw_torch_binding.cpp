@@ -14,7 +14,7 @@
 //   * candidate_buffer/indices rows hold exactly the support (kappa entries),
 //     so fw_backward needs no zero-initialised [N,K] buffer.
 // Extra functions used by the autograd layer (fwloss_b200 package):
-//   fused_fwd_bwd, scale_grad, loss_reduce, shard_scan, shard_solve, and the
+//   fused_fwd_bwd, forward_rows, scale_grad, loss_reduce, shard_scan, shard_solve, and the
 //   LM-head pieces shard_scan_into, label_logits, lmhead_fused_scan, chunks_solve,
 //   sparse_grad_hidden, sparse_grad_weight.
 #include <torch/extension.h>
@@ -226,6 +226,41 @@ std::vector<torch::Tensor> fused_fwd_bwd(torch::Tensor logits, torch::Tensor tar
                                   losses.data_ptr<float>(), kappa.data_ptr<int32_t>(), st, cur_stream()),
            "fw_fused_fwd_bwd");
   return {grad, H, losses, kappa};
+}
+
+// Forward only (new): (H, losses, kappa) without a gradient -- the logits are
+// read once and nothing of their size is written.  H and losses float32
+// (float64 for float64 logits).
+std::vector<torch::Tensor> forward_rows(torch::Tensor logits, torch::Tensor targets,
+                                        c10::optional<torch::Tensor> status) {
+  check_logits(logits, true);
+  const c10::cuda::CUDAGuard guard(logits.device());
+  const int64_t N = logits.size(0), K = logits.size(1);
+  check_targets(targets, N, logits);
+  int64_t ld = K;
+  auto z = rows_view(logits, &ld);
+  auto y = targets.contiguous();
+  const bool f64 = z.scalar_type() == torch::kFloat64;
+  const auto out_t = f64 ? torch::kFloat64 : torch::kFloat32;
+  auto H = torch::empty({N}, logits.options().dtype(out_t));
+  auto losses = torch::empty({N}, logits.options().dtype(out_t));
+  auto kappa = torch::empty({N}, i32(logits));
+  int32_t* st = nullptr;
+  if (status.has_value()) {
+    TORCH_CHECK(status->is_cuda() && status->scalar_type() == torch::kInt32 && status->numel() >= 1,
+                "status must be an int32 CUDA tensor");
+    st = status->data_ptr<int32_t>();
+  }
+  if (f64) {
+    check_rc(fw_forward_rows_f64(z.data_ptr<double>(), y.data_ptr<int64_t>(), N, K, ld, H.data_ptr<double>(),
+                                 losses.data_ptr<double>(), kappa.data_ptr<int32_t>(), st, cur_stream()),
+             "fw_forward_rows_f64");
+    return {H, losses, kappa};
+  }
+  check_rc(fw_forward_rows(dtype_code(z), z.data_ptr(), y.data_ptr<int64_t>(), N, K, ld, H.data_ptr<float>(),
+                           losses.data_ptr<float>(), kappa.data_ptr<int32_t>(), st, cur_stream()),
+           "fw_forward_rows");
+  return {H, losses, kappa};
 }
 
 // grad (in place) *= grad_output[per_row ? r : 0] / assumed_scale.
@@ -585,6 +620,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fw_backward_small", &fw_backward_small, "FW backward from the bool mask (mean scaling)");
   m.def("fused_fwd_bwd", &fused_fwd_bwd, "fused forward+backward: (grad, H, losses, kappa)",
         py::arg("logits"), py::arg("targets"), py::arg("grad_scale"), py::arg("status") = py::none());
+  m.def("forward_rows", &forward_rows, "forward only, no gradient: (H, losses, kappa)", py::arg("logits"),
+        py::arg("targets"), py::arg("status") = py::none());
   m.def("scale_grad", &scale_grad, "in-place grad scaling by a device-side grad_output");
   m.def("fused_fwd_bwd_cols", &fused_fwd_bwd_cols,
         "fused forward+backward listing the support columns: (grad, H, losses, kappa, sup_cols)",

@@ -133,6 +133,8 @@ __device__ __forceinline__ void warp_tier_nonfinite(const RowArgs& a, int64_t ro
       a.cand_idx[row * a.C] = jstar;
       if (a.cand_count) a.cand_count[row] = 1;
     }
+  } else if (OUT == kOutNone) {
+    // forward only: no per-element output
   } else {  // kOutShard: zero gradient shard (if any), summary of a non-finite row
     if (a.grad) {
       T* gr = static_cast<T*>(a.grad) + row * a.ld;
@@ -180,7 +182,7 @@ __global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS * El
   constexpr int NV = NS * EPS;          // register values per lane
   constexpr int RPW = 32 / G;           // rows per warp
   constexpr int CAPG = kWarpListCap / RPW;
-  static_assert(OUT == kOutGrad || OUT == kOutGradCols || sizeof(T) == 4,
+  static_assert(OUT == kOutGrad || OUT == kOutGradCols || OUT == kOutNone || sizeof(T) == 4,
                 "mask/candidate/shard outputs are fp32-only");
   __shared__ float s_list[kWarpTierWarps][kWarpListCap];
   const int lane = threadIdx.x & 31;
@@ -361,6 +363,8 @@ __global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS * El
         rec[3] = -1;
       }
       continue;
+    } else if (OUT == kOutNone) {
+      // forward only: H, loss and kappa below
     } else {  // kOutCand
       int cnt = 0;
 #pragma unroll

@@ -4,7 +4,9 @@ Every wrapper takes CUDA tensors, passes raw device pointers, sizes and the
 current torch stream of the tensors' device, and raises FWError on a non-zero
 return code.  Nothing here computes anything: all work happens in the CUDA
 kernels behind the C ABI.  This is the path the GPU parity tests use, and the
-template for a non-Python binding (see INTEGRATION.md at the repository root).
+template for a binding from another host language (cgo, JNI, N-API): one
+foreign-function prototype per declaration of the header, raw pointers in,
+an int status out.
 """
 import ctypes
 import os
@@ -60,6 +62,8 @@ _SIGS["fw_loss_reduce_f64"] = ([_P, _I64, ctypes.c_double, _P, _P], ctypes.c_int
 _SIGS["fw_sparse_grad_hidden_shard"] = ([ctypes.c_int, _P, _I64, _I64, _I64, _P, ctypes.c_int, _P, _P, _I64,
                                          ctypes.c_float, _P, ctypes.c_int, _P, _P], ctypes.c_int)
 _SIGS["fw_weight_grad_keys_shard"] = ([_P, ctypes.c_int, _P, _P, _I64, _I64, _I64, _P, _P], ctypes.c_int)
+_SIGS["fw_forward_rows"] = ([ctypes.c_int, _P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P], ctypes.c_int)
+_SIGS["fw_forward_rows_f64"] = ([_P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P], ctypes.c_int)
 _SIGS["fw_lmhead_fused_loss_noalloc"] = ([ctypes.c_int, _P, _I64, _I64, _P, _I64, ctypes.c_int, _P, ctypes.c_int,
                                           _P, _P, _P, _P, _P, _P, _P, _P, _P], ctypes.c_int)
 DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
@@ -143,6 +147,27 @@ def fused_fwd_bwd(z, y, grad_scale, grad=None, status=None):
                                             _ptr(kappa), _ptr(status), _stream(z))
         _check(rc, "fw_fused_fwd_bwd")
     return grad, H, loss, kappa
+
+
+def forward_rows(z, y, status=None):
+    """(H, loss, kappa) without a gradient (fw_forward_rows; float64 logits:
+    fw_forward_rows_f64 with fp64 H and loss)."""
+    z, ld = _rows(z, any_float=True)
+    B, C = z.shape
+    f64 = z.dtype == torch.float64
+    H = torch.empty(B, dtype=torch.float64 if f64 else torch.float32, device=z.device)
+    loss = torch.empty(B, dtype=H.dtype, device=z.device)
+    kappa = torch.empty(B, dtype=torch.int32, device=z.device)
+    lib = load()
+    with torch.cuda.device(z.device):
+        if f64:
+            rc = lib.fw_forward_rows_f64(_ptr(z), _ptr(y), B, C, ld, _ptr(H), _ptr(loss), _ptr(kappa),
+                                         _ptr(status), _stream(z))
+        else:
+            rc = lib.fw_forward_rows(DTYPE_CODES[z.dtype], _ptr(z), _ptr(y), B, C, ld, _ptr(H), _ptr(loss),
+                                     _ptr(kappa), _ptr(status), _stream(z))
+        _check(rc, "fw_forward_rows")
+    return H, loss, kappa
 
 
 def forward_mask(z, y, status=None):

@@ -50,7 +50,11 @@ def sharded_familywise_loss(local_logits, local_target, global_batch, group=None
 
     Every rank must call it (it contains one all-reduce).  The returned 0-d
     tensor is the global mean; backward gives this rank's rows of the global
-    gradient.
+    gradient.  Without a possible gradient (no_grad, or logits that do not
+    require grad) the forward-only kernel runs (no gradient is written).
     """
     _check_inputs(local_logits, local_target)
+    if not (torch.is_grad_enabled() and local_logits.requires_grad):
+        _, losses, _ = ext().forward_rows(local_logits.detach(), local_target, None)
+        return reduce_loss_sum(ext().loss_reduce(losses, 1.0 / int(global_batch)), group)
     return _ShardedFW.apply(local_logits, local_target, int(global_batch), group)

@@ -12,12 +12,30 @@ Unlike the CPU version, backward never synchronises with the host: the
 upstream gradient is read on the device, and rows whose factor is exactly 1
 (the usual `loss.backward()`) are left untouched.  "none" is supported in
 addition to "mean" and "sum".
+
+When no gradient can be asked for (under torch.no_grad(), or logits that do
+not require grad -- evaluation with FWLoss), the forward-only kernel runs
+instead: same H, losses and kappa, but the logits are read once and no
+gradient is written (half the HBM bytes of the fused kernel).  The reference
+computes the gradient in forward either way (src/cpu/fw_cpu.cpp:722-733).
 """
 import torch
 
 from ._native import ext
 
 _REDUCTIONS = ("mean", "sum", "none")
+
+
+def _wants_grad(logits):
+    return torch.is_grad_enabled() and logits.requires_grad
+
+
+def _forward_only(logits, target, status):
+    """(losses in the logits' dtype, H, kappa) without a gradient."""
+    H, losses, kappa = ext().forward_rows(logits.detach(), target, status)
+    if logits.dtype not in (torch.float32, torch.float64):
+        losses = losses.to(logits.dtype)
+    return losses, H, kappa
 
 
 def _check_inputs(logits, target):
@@ -138,17 +156,27 @@ def familywise_loss(logits, target, reduction="mean", status=None):
         raise ValueError(f"Invalid reduction mode: {reduction}")
     _check_inputs(logits, target)
     n = logits.shape[0]
+    scale = (1.0 / n if n else float("nan")) if reduction == "mean" else 1.0
+    if not _wants_grad(logits):
+        if reduction == "none":
+            return _forward_only(logits, target, status)[0]
+        _, losses, _ = ext().forward_rows(logits.detach(), target, status)  # fp32 (fp64) losses
+        out = ext().loss_reduce(losses, scale)
+        return out if out.dtype == logits.dtype else out.to(logits.dtype)
     if reduction == "none":
         if logits.dtype == torch.float64 or logits.shape[1] <= LISTED_MIN_CLASSES:
             return _FWRows.apply(logits, target, 1.0, status)[0]
         return _FWRowsListed.apply(logits, target, status)[0]
-    scale = (1.0 / n if n else float("nan")) if reduction == "mean" else 1.0
     return _FWReduced.apply(logits, target, scale, status)
 
 
 def fw_rows(logits, target, assumed_scale=1.0, status=None):
-    """(losses [N] differentiable, H [N] fp32 (fp64 for float64 logits), kappa [N] int32)."""
+    """(losses [N] differentiable, H [N] fp32 (fp64 for float64 logits), kappa [N] int32).
+    Without a possible gradient (no_grad, or logits not requiring grad) the
+    forward-only kernel runs and the losses are plain tensors."""
     _check_inputs(logits, target)
+    if not _wants_grad(logits):
+        return _forward_only(logits, target, status)
     return _FWRows.apply(logits, target, float(assumed_scale), status)
 
 

@@ -181,6 +181,26 @@ FWB_API int fw_scale_grad(float* grad, const float* grad_output, int per_row,
                   float assumed_scale, int64_t B, int64_t C, int64_t ld,
                   void* stream);
 
+/*
+ * Forward only: H, loss and kappa per row, no gradient (z is read once and
+ * nothing of size C is written: half the HBM bytes of fw_fused_fwd_bwd).
+ * Same threshold search, so H, loss and kappa equal those of
+ * fw_fused_fwd_bwd bit for bit.  `dtype` is FWB_DTYPE_F32, _BF16 or _F16.
+ * Replaces the forward of FWLoss when no gradient is wanted (evaluation,
+ * torch.no_grad; reference_impl.py:11-35) and the forward of the reference
+ * CUDA path without its [N, K] mask or candidate buffers
+ * (src/cuda/fw_radix_argmax.cu:1381-1414, :1417-1496).
+ */
+FWB_API int fw_forward_rows(int dtype, const void* z, const int64_t* y, int64_t B, int64_t C,
+                            int64_t ld, float* H, float* loss, int32_t* kappa, int32_t* status,
+                            void* stream);
+
+/* fw_forward_rows for float64 logits (fp64 H and loss), the forward of the
+ * reference CPU kernel's float64 branch (src/cpu/fw_cpu.cpp:698-704). */
+FWB_API int fw_forward_rows_f64(const double* z, const int64_t* y, int64_t B, int64_t C,
+                                int64_t ld, double* H, double* loss, int32_t* kappa,
+                                int32_t* status, void* stream);
+
 /* fw_scale_grad for a gradient of element type `dtype` (FWB_DTYPE_*). */
 FWB_API int fw_scale_grad_typed(int dtype, void* grad, const float* grad_output, int per_row,
                                 float assumed_scale, int64_t B, int64_t C, int64_t ld,
@@ -372,11 +392,14 @@ FWB_API int fw_loss_reduce_f64(const double* loss, int64_t B, double scale, doub
  * that forbid allocation after start-up, FFI hosts that only hold the buffers
  * handed to them.  The workspace needs
  *     round_up(nchunks * B * (4 + K), 64) + round_up(nchunks * B * K, 64) + B
- * 4-byte words, at most FWB_NOALLOC_SCRATCH_BYTES / 4; larger problems
- * return FWB_E_CAPACITY (e.g. B = 8192, nchunks = 8, K = 16 fits).  The array
- * is FWB_NOALLOC_SCRATCH_BYTES on every GPU that loads the library, held until
- * exit.  The first call on a device looks up the array's address with that
- * device current; make it before any stream capture.  All calls share the
+ * 4-byte words, at most FWB_NOALLOC_SCRATCH_BYTES / 4, and nchunks * K <= 256
+ * (fw_chunks_solve's limit); other problems return FWB_E_CAPACITY before any
+ * kernel runs (e.g. B = 8192, nchunks = 8, K = 16 fits).  The array is
+ * FWB_NOALLOC_SCRATCH_BYTES on every GPU that loads the library, held until
+ * exit.  The first call in a CUDA context looks up the array's address with
+ * that context current and caches it under the context's unique id (a device
+ * reset makes a new context, whose first call looks it up again); make the
+ * first call on each device before any stream capture.  All calls share the
  * array: calls that overlap on the GPU race.  No counterpart in the reference.
  */
 #define FWB_NOALLOC_SCRATCH_BYTES (16 * 1024 * 1024)

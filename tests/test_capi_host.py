@@ -58,6 +58,15 @@ def test_argument_checks_without_device():
     assert lib.fw_forward_candidates(dummy, dummy, 4, 10, 10, P, P, P, P, dummy, P, P, P) == 2
     assert lib.fw_backward_mask(P, dummy, dummy, 4, 10, 1.0, dummy, P, P) == 2
     assert lib.fw_loss_reduce(dummy, 4, 1.0, P, P) == 2
+    # forward only: dtype, shape and pointer checks; an empty batch is a no-op
+    assert lib.fw_forward_rows(7, dummy, dummy, 4, 10, 10, P, P, P, P, P) == 5
+    assert lib.fw_forward_rows(0, dummy, dummy, 4, 10, 9, P, P, P, P, P) == 1
+    assert lib.fw_forward_rows(1, P, dummy, 4, 10, 10, P, P, P, P, P) == 2
+    assert lib.fw_forward_rows(2, dummy, P, 4, 10, 10, P, P, P, P, P) == 2
+    assert lib.fw_forward_rows(0, P, P, 0, 10, 10, P, P, P, P, P) == 0
+    assert lib.fw_forward_rows_f64(dummy, dummy, -1, 10, 10, P, P, P, P, P) == 1
+    assert lib.fw_forward_rows_f64(P, dummy, 4, 10, 10, P, P, P, P, P) == 2
+    assert lib.fw_forward_rows_f64(P, P, 0, 10, 10, P, P, P, P, P) == 0
     # an empty batch is a valid no-op (no launch)
     assert lib.fw_fused_fwd_bwd(P, P, 0, 10, 10, 1.0, P, P, P, P, P, P) == 0
     # float64 entry points: same checks
@@ -108,3 +117,6 @@ def test_argument_checks_of_the_later_entry_points():
     assert lib.fw_lmhead_fused_loss_noalloc(1, d, 4, 64, d, 1000, 0, cs, 8, d, P, d, P, d, d, d, P, P) == 4
     assert lib.fw_lmhead_fused_loss_noalloc(1, d, 1 << 20, 64, d, 1000, 2, cs, 64, d, P, d, P, d, d, d, P, P) == 4
     assert lib.fw_lmhead_fused_loss_noalloc(1, d, -1, 64, d, 1000, 2, cs, 8, d, P, d, P, d, d, d, P, P) == 1
+    # nchunks * K above the chunk solve's 256-entry list: refused before any kernel is queued
+    cs16 = (ctypes.c_int64 * 17)(*[256 * i for i in range(17)])
+    assert lib.fw_lmhead_fused_loss_noalloc(1, d, 4, 64, d, 4096, 16, cs16, 32, d, P, d, P, d, d, d, P, P) == 4

@@ -131,3 +131,15 @@ def test_no_alloc_rejects_problems_beyond_its_workspace():
     assert _no_alloc(lib, hidden, weight, target, cs, K, out, stream) == FWB_E_CAPACITY
     torch.cuda.synchronize()
     assert int(out["kappa"].min()) == -7 and int(out["kappa"].max()) == -7  # nothing was written
+    # a small batch whose chunk lists exceed the solve's 256 entries per row
+    # (nchunks * K = 16 * 32): refused before the scan touches the array
+    B, C, K = 64, 16 * 256, 32
+    cs = tile_col_start(C, 16)
+    n = len(cs) - 1
+    assert n * K > 256
+    hidden, weight, target = _inputs(B, D, C, 4)
+    out = _outputs(B, n, K)
+    assert _no_alloc(lib, hidden, weight, target, cs, K, out, stream) == FWB_E_CAPACITY
+    torch.cuda.synchronize()
+    assert int(out["kappa"].min()) == -7 and int(out["kappa"].max()) == -7
+    assert int(out["status"][0]) == 0
