@@ -1,28 +1,33 @@
 #!/usr/bin/env python
 """FWLoss forward+backward throughput on B200 (rows/s, HBM roofline).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config cfgX]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config cfgX] [--weak]
 
 Default workload: cfg2 of the reference's benchmark set -- B=4096 rows x
 C=32000 classes, fp32 Student-t(3)*2 logits, int64 labels (seeded synthetic
 data, fwloss_b200.workloads).  A step is one fused forward+backward of the
 whole batch (threshold search, per-row loss, dense gradient) plus the
-deterministic loss reduction; with N > 1 ranks each rank runs its own batch
-of B rows (weak scaling, rows are independent) and the global mean is
-combined by one scalar NCCL all-reduce per step (issued asynchronously so it
-overlaps the next step's kernel; all are complete before the timed region
-closes).
+deterministic loss reduction.  With N > 1 ranks (torchrun, one per GPU) the
+batch's B rows are split into contiguous row blocks (strong scaling, the
+metric's fixed B; --weak gives every rank B rows of its own), every rank runs
+the same step on its block with the gradient scaled by 1/B, and the global
+mean is combined by one scalar NCCL all-reduce per step, issued
+asynchronously so that it runs under the next step's kernel.  The K timed
+steps are captured once in a CUDA graph (kernels and NCCL call).
 
 Printed JSON line (rank 0):
   value     rows/s of the whole job, inputs resident in HBM, device-timed with
             CUDA events over exactly K steps (barrier + synchronize on both
             sides, max over ranks).
-  e2e       same metric through the public autograd API with the logits and
-            labels copied from pinned host memory every step and the loss read
-            back (host<->device copies inside the timed region).
+  e2e       same metric through the public API -- familywise_loss on one GPU,
+            fwloss_b200.distributed.sharded_familywise_loss on N -- with the
+            logits and labels copied from pinned host memory every step and
+            the loss read back (host<->device copies inside the timed region).
   roofline  the fused kernel alone: algorithmic bytes per launch
             (B * (8C + 12): read logits, write gradient, label, loss) over its
             CUDA-event average duration, against the measured HBM copy peak.
+  forward_only  the same for the forward-only kernel (B * (4C + 12) bytes).
+  weak      (N > 1) the weak-scaling figure: every rank B rows.
   cpu_baseline  the reference's own CPU implementation (src/cpu/fw_cpu.cpp,
             compiled by oracle/build.py) on this host's cores, on a bounded
             sample of the same workload (rank 0, N = 1 only).
@@ -64,9 +69,10 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-graph", action="store_true", help="launch steps eagerly")
-    p.add_argument("--strong", action="store_true",
-                   help="rows mode: split the configuration's B rows across the ranks (strong scaling) instead "
-                        "of giving every rank B rows of its own (weak scaling, the default)")
+    p.add_argument("--weak", action="store_true",
+                   help="rows mode: give every rank B rows of its own (weak scaling) instead of splitting the "
+                        "configuration's B rows across the ranks (strong scaling, the default; the weak figure "
+                        "is also reported under 'weak' at N > 1)")
     p.add_argument("--mode", default="rows", choices=["rows", "class-sharded", "lm-head"],
                    help="rows: rows sharded across GPUs (default); class-sharded: every GPU holds a "
                         "column shard of every row (vocabulary-parallel), cfg4 shape; lm-head: "
@@ -82,17 +88,28 @@ def parse():
     return p.parse_args()
 
 
-def workload_desc(name, B, C, world, esize=4):
+def bench_config(name, world, strong=True, esize=4):
+    """The `config` object of the bench line, identical in both arms for the
+    same (configuration, N, scaling): strong scaling splits the
+    configuration's B rows across the N ranks, weak scaling gives every rank
+    B rows."""
+    from fwloss_b200 import workloads
+
+    B_cfg, C = workloads.shape_of(name)
+    Bg = B_cfg if (strong or world == 1) else B_cfg * world
+    rows = -(-B_cfg // world) if (strong and world > 1) else B_cfg  # largest rank block
     kinds = {"cfg0": "N(0,1)", "cfg1": "N(0,1) +4 at label", "cfg2": "Student-t(3) x2",
              "cfg3": "8 levels + 1% signed zeros", "cfg4": "N(0,1) +8 at a non-label class"}
+    per = rows * C * esize
     return {
-        "workload": f"{name}: FWLoss fwd+bwd, B={B} x C={C}, {dict([(8, 'fp64'), (4, 'fp32'), (2, '16-bit')])[esize]} "
-                    f"logits {kinds.get(name, 'N(0,1)' if name.startswith('gauss') else '')}, int64 labels",
-        "rows_per_gpu": B, "classes": C, "global_batch": B * world,
+        "workload": f"{name}: FWLoss fwd+bwd, B={B_cfg} x C={C}, "
+                    f"{dict([(8, 'fp64'), (4, 'fp32'), (2, '16-bit')])[esize]} logits "
+                    f"{kinds.get(name, 'N(0,1)' if name.startswith('gauss') else '')}, int64 labels",
+        "rows_per_gpu": rows, "classes": C, "global_batch": Bg,
         "parallelism": f"row-sharded dp{world}" + (" + scalar NCCL all-reduce" if world > 1 else ""),
-        "l2": f"inputs {B * C * esize / 1e6:.1f} MB logits + {B * C * esize / 1e6:.1f} MB gradient per step"
-              + (" (> 3x the 126 MB L2, no flush needed)" if B * C * esize > 3 * L2_BYTES else
-                 f" (rotating over {min(64, -(-3 * L2_BYTES // (B * C * esize)))} input copies)"),
+        "l2": f"inputs {per / 1e6:.1f} MB logits + {per / 1e6:.1f} MB gradient per step and GPU"
+              + (" (> 3x the 126 MB L2, no flush needed)" if per > 3 * L2_BYTES else
+                 f" (rotating over {min(64, -(-3 * L2_BYTES // per))} input copies)"),
     }
 
 
@@ -230,6 +247,7 @@ def cpu_baseline(name, B, C, seconds, f64=False):
 
 def run_reference(a):
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(a.gpus)))
     if rank != 0:
         return 0
     import torch
@@ -261,13 +279,14 @@ def run_reference(a):
     el = time.perf_counter() - t
     value = rows * a.steps / el
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": a.gpus,
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * el / a.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": workload_desc(a.config, rows, C, 1),
+        "higher_is_better": True, "scaling": "strong" if not a.weak else "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic", "config": bench_config(a.config, world, not a.weak),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
-                         "sample": f"{rows} rows of {a.config} per step (reference src/cpu/fw_cpu.cpp, "
-                                   f"familywise_loss mean + backward, simd={mod.simd()})"},
+                         "sample": f"{rows} of the {B} rows of {a.config} per step (reference "
+                                   f"src/cpu/fw_cpu.cpp, familywise_loss mean + backward, simd={mod.simd()}; "
+                                   f"host cores only, the same whatever the GPU count)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
     }
@@ -315,12 +334,62 @@ def run_reference_cuda(a):
     print(json.dumps({
         "impl": "reference-cuda", "metric": METRIC, "value": B / (ms / 1e3), "unit": UNIT, "n_gpus": 1,
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_desc(a.config, B, C, 1),
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": bench_config(a.config, 1),
         "path": "fw_forward_small + fw_backward_small" if C < 10000 else "fw_forward + fw_backward",
         "hbm": {"alg_bytes_per_step": alg, "achieved_gbs": alg / (ms / 1e3) / 1e9,
                 "frac": alg / (ms / 1e3) / 1e9 / peak, "peak": peak, "peak_kind": peak_kind},
     }), flush=True)
     return 0
+
+
+def _rank_inputs(a, world, rank, dev, strong):
+    """(z_local, y_local) on the device and (global rows, rows of the
+    configuration).  Strong scaling: rank 0 draws the configuration's whole
+    batch on the host and broadcasts it over NCCL; every rank keeps its
+    contiguous row block (fwloss_b200.distributed.shard_rows).  Weak scaling:
+    every rank draws a batch of its own (workloads.make_rank)."""
+    import torch
+    import torch.distributed as dist
+
+    from fwloss_b200 import workloads
+    from fwloss_b200.distributed import shard_rows
+
+    B_cfg, C = workloads.shape_of(a.config)
+    if world == 1 or not strong:
+        z, y = workloads.make_rank(a.config, rank)
+        return z.to(dev), y.to(dev), B_cfg * world, B_cfg
+    if rank == 0:
+        z, y = workloads.make(a.config)
+        z, y = z.to(dev), y.to(dev)
+    else:
+        z = torch.empty((B_cfg, C), dtype=torch.float32, device=dev)
+        y = torch.empty((B_cfg,), dtype=torch.int64, device=dev)
+    dist.broadcast(z, 0)
+    dist.broadcast(y, 0)
+    lo, hi = shard_rows(B_cfg, rank, world)
+    zl, yl = z[lo:hi].clone(), y[lo:hi].clone()
+    del z, y
+    torch.cuda.empty_cache()
+    return zl, yl, B_cfg, B_cfg
+
+
+def _graph_of(fn, dev, warm_fn=None):
+    """fn() captured once in a CUDA graph, after warm_fn() (or fn()) ran
+    eagerly on the capture stream; returns the graph.  Raises RuntimeError
+    when capture is not possible."""
+    import torch
+
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        (warm_fn or fn)()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    torch.cuda.synchronize(dev)
+    return g
 
 
 def run_ours(a):
@@ -329,6 +398,7 @@ def run_ours(a):
 
     from fwloss_b200 import familywise_loss, workloads
     from fwloss_b200._native import ext
+    from fwloss_b200.distributed import sharded_familywise_loss
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -339,112 +409,86 @@ def run_ours(a):
     dev = torch.device("cuda", local)
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    B, C = workloads.shape_of(a.config)
+    strong = not a.weak
+    B_cfg, C = workloads.shape_of(a.config)
     fw = ext()
-
-    # inputs: weak scaling: rank 0 gets the configuration itself, other ranks
-    # the same recipe with their own seed (every rank owns B distinct rows);
-    # strong scaling: every rank takes its contiguous block of the
-    # configuration's B rows
-    if a.strong:
-        from fwloss_b200.distributed import shard_rows
-
-        Bg = B
-        lo, hi = shard_rows(B, rank, world)
-        z_all, y_all = workloads.make(a.config)
-        z_cpu, y_cpu = z_all[lo:hi].contiguous(), y_all[lo:hi].contiguous()
-        del z_all, y_all
-        B = hi - lo
-    else:
-        z_cpu, y_cpu = workloads.make_rank(a.config, rank)
-        Bg = B * world
+    z_dev, y, Bg, _ = _rank_inputs(a, world, rank, dev, strong)
+    B = z_dev.shape[0]
     tdt = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16, "f64": torch.float64}[a.dtype]
     esize = torch.tensor([], dtype=tdt).element_size()
-    z_cpu = z_cpu.to(tdt)
-    # inputs larger than L2 (126 MB): small configurations rotate over enough
-    # copies that 3x the L2 size is touched between two uses of one copy
+    z_dev = z_dev.to(tdt)
+    # inputs larger than L2 (126 MB): small batches rotate over enough copies
+    # that 3x the L2 size is touched between two uses of one copy
     copies = 1 if B * C * esize > 3 * L2_BYTES else min(64, -(-3 * L2_BYTES // (B * C * esize)))
-    zs = [z_cpu.to(dev) for _ in range(copies)]
-    y = y_cpu.to(dev)
+    zs = [z_dev] + [z_dev.clone() for _ in range(copies - 1)]
     scale = 1.0 / Bg
     stream = torch.cuda.current_stream(dev)
 
-    pending = []  # multi-GPU: async all-reduce handles of the current timed loop
+    def steps(n, inputs=zs, rows_y=y, sc=scale, forward_only=False):
+        """n steps: the fused forward+backward (or the forward-only kernel),
+        the deterministic loss reduction, and with N > 1 ranks the scalar
+        all-reduce, issued asynchronously so that it runs under the next
+        step's kernel; the last one is waited for before returning."""
+        pend = None
+        for i in range(n):
+            zi = inputs[i % len(inputs)]
+            if forward_only:
+                _, loss, _ = fw.forward_rows(zi, rows_y, None)
+            else:
+                _, _, loss, _ = fw.fused_fwd_bwd(zi, rows_y, sc)
+            s = fw.loss_reduce(loss, sc)
+            if world > 1:
+                if pend is not None:
+                    pend.wait()
+                pend = dist.all_reduce(s, async_op=True)
+        if pend is not None:
+            pend.wait()
 
-    def step(i):
-        grad, H, loss, kappa = fw.fused_fwd_bwd(zs[i % copies], y, scale)
-        s = fw.loss_reduce(loss, scale)
-        if world > 1:
-            # the scalar exchange overlaps the next step's kernel; every handle is
-            # waited on before the closing event of the timed region
-            pending.append((dist.all_reduce(s, async_op=True), s))
-        return s
+    def kernels(n, inputs=zs, rows_y=y, forward_only=False):
+        for i in range(n):
+            if forward_only:
+                fw.forward_rows(inputs[i % len(inputs)], rows_y, None)
+            else:
+                fw.fused_fwd_bwd(inputs[i % len(inputs)], rows_y, scale)
 
-    def drain():
-        for work, _ in pending:
-            work.wait()
-        pending.clear()
-
-    def kernel_only(i):
-        fw.fused_fwd_bwd(zs[i % copies], y, scale)
-
-    # single GPU: replay steps from CUDA graphs (same kernels, no Python
-    # launch overhead); multi-GPU steps stay eager (they contain NCCL).  Small
-    # configurations (rotating input copies, steps of a few microseconds) put
-    # all K timed steps into one graph, so that the graph launch gap between
-    # steps is not timed; large ones replay one graph per step.
-    use_graph = world == 1 and not a.no_graph
-    run_steps = run_kernels = None
-    if use_graph:
-        side = torch.cuda.Stream(dev)
-        side.wait_stream(stream)
-        with torch.cuda.stream(side):
-            for i in range(copies):
-                step(i)
-                kernel_only(i)
-        stream.wait_stream(side)
-        torch.cuda.synchronize(dev)
-        if copies > 1:
-            def capture(fn, n):
-                g = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g):
-                    for i in range(n):
-                        fn(i)
-                return g
-
-            g_all, g_kern_all = capture(step, a.steps), capture(kernel_only, a.steps)
-            run_steps, run_kernels = g_all.replay, g_kern_all.replay
-        g_step, g_kern = [], []
-        for i in range(copies):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                step(i)
-            g_step.append(g)
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                kernel_only(i)
-            g_kern.append(g)
-        run_step = lambda i: g_step[i % copies].replay()  # noqa: E731
-        run_kernel = lambda i: g_kern[i % copies].replay()  # noqa: E731
+    # The K timed steps are captured once in a CUDA graph (the same kernels and
+    # NCCL call, without Python launch overhead); --no-graph runs them eagerly.
+    warm = max(3, a.warmup)
+    launch_mode = "eager"
+    run_steps = lambda: steps(a.steps)  # noqa: E731
+    g_steps = None
+    if not a.no_graph:
+        try:
+            g_steps = _graph_of(lambda: steps(a.steps), dev, warm_fn=lambda: steps(warm))
+            run_steps, launch_mode = g_steps.replay, "one CUDA graph of the K timed steps"
+        except RuntimeError as ex:  # capture not possible here: time eagerly, say so
+            launch_mode = f"eager (graph capture failed: {str(ex)[:120]})"
+            torch.cuda.synchronize(dev)
     else:
-        run_step, run_kernel = step, kernel_only
-    if run_steps is None:
-        def run_steps():
-            for i in range(a.steps):
-                run_step(i)
-
-        def run_kernels():
-            for i in range(a.steps):
-                run_kernel(i)
-
-    for i in range(a.warmup):
-        run_step(i)
-    drain()
+        steps(warm)
+    run_steps()  # untimed warm replay
     torch.cuda.synchronize(dev)
 
     def barrier():
         if world > 1:
             dist.barrier()
+
+    def max_over_ranks(ms):
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(fn):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize(dev)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1))
 
     phys = local
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
@@ -453,42 +497,68 @@ def run_ours(a):
             phys = int(vis.split(",")[local])
         except (ValueError, IndexError):
             phys = local
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(phys) as clk:
-        barrier()
-        torch.cuda.synchronize(dev)
-        e0.record(stream)
-        run_steps()
-        drain()
-        e1.record(stream)
-        torch.cuda.synchronize(dev)
-        barrier()
-    ms = e0.elapsed_time(e1)
+        ms = timed(run_steps)
     clocks = clk.summary()
-    t = torch.tensor([ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
     value = Bg * a.steps / (ms / 1e3)
 
-    # roofline: the fused kernel alone, back to back on the launching stream
-    kd0, kd1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    for i in range(3):
-        run_kernel(i)
-    torch.cuda.synchronize(dev)
-    kd0.record(stream)
-    run_kernels()
-    kd1.record(stream)
-    torch.cuda.synchronize(dev)
-    k_ms = kd0.elapsed_time(kd1) / a.steps
-    alg_bytes = B * (2 * esize * C + (16 if esize == 8 else 12))  # + label, loss
+    # roofline: the fused kernel alone, K launches back to back (one graph)
+    def kernel_ms(forward_only):
+        fn = lambda: kernels(a.steps, forward_only=forward_only)  # noqa: E731
+        if not a.no_graph:
+            try:
+                fn = _graph_of(fn, dev, warm_fn=lambda: kernels(3, forward_only=forward_only)).replay
+            except RuntimeError:
+                pass
+        fn()
+        torch.cuda.synchronize(dev)
+        kd0, kd1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        kd0.record(stream)
+        fn()
+        kd1.record(stream)
+        torch.cuda.synchronize(dev)
+        return kd0.elapsed_time(kd1) / a.steps
+
+    k_ms = kernel_ms(False)
+    tail = 16 if esize == 8 else 12  # label + loss (fp64 loss for fp64 logits)
+    alg_bytes = B * (2 * esize * C + tail)
     achieved = alg_bytes / (k_ms / 1e3) / 1e9
     peak, peak_kind = measured_peak()
 
-    # e2e: public autograd API, host buffers, copies inside the timed region
+    # forward only (no gradient): the kernel a no_grad / evaluation call runs
+    f_ms = kernel_ms(True)
+    f_bytes = B * (esize * C + tail)
+    fwd = {"kernel_ms": f_ms, "alg_bytes_per_launch": f_bytes, "achieved": f_bytes / (f_ms / 1e3) / 1e9,
+           "frac": f_bytes / (f_ms / 1e3) / 1e9 / peak, "unit": "GB/s",
+           "rows_per_s": Bg / (f_ms / 1e3) if world == 1 else None,
+           "what": "fw_forward_rows: H, loss and kappa, logits read once, no gradient written"}
+
+    # weak scaling (N > 1): every rank a full batch of the configuration's
+    # B rows (its own row block tiled up to B rows), same step
+    weak = None
+    if world > 1 and strong:
+        reps = -(-B_cfg // B)
+        zw = zs[0].repeat(reps, 1)[:B_cfg].contiguous()
+        yw = y.repeat(reps)[:B_cfg].contiguous()
+        fnw = lambda: steps(a.steps, inputs=[zw], rows_y=yw, sc=1.0 / (B_cfg * world))  # noqa: E731
+        if launch_mode.startswith("one CUDA graph"):
+            fnw = _graph_of(fnw, dev, warm_fn=lambda: steps(3, inputs=[zw], rows_y=yw)).replay
+        fnw()
+        torch.cuda.synchronize(dev)
+        w_ms = timed(fnw)
+        weak = {"value": B_cfg * world * a.steps / (w_ms / 1e3), "unit": UNIT, "ms_per_step": w_ms / a.steps,
+                "rows_per_gpu": B_cfg, "global_batch": B_cfg * world,
+                "what": "weak scaling: every rank runs the configuration's full batch size"}
+        del fnw, zw, yw  # the graph (it holds NCCL calls) and its inputs
+        torch.cuda.synchronize(dev)
+
+    # e2e: the public API with host buffers; every step copies this rank's
+    # logits and labels from pinned host memory and reads the loss back.
+    # One rank: familywise_loss(mean).backward(); N > 1:
+    # sharded_familywise_loss(rows, labels, global batch).backward().
     ne = a.e2e_steps or min(a.steps, 10)
-    zh = z_cpu.pin_memory()
-    yh = y_cpu.pin_memory()
+    zh = zs[0].cpu().pin_memory()
+    yh = y.cpu().pin_memory()
     zd = torch.empty_like(zs[0]).requires_grad_(True)
     yd = torch.empty_like(y)
     lh = torch.empty(ne + a.warmup, dtype=torch.float32).pin_memory()
@@ -498,33 +568,28 @@ def run_ours(a):
             zd.copy_(zh, non_blocking=True)
             yd.copy_(yh, non_blocking=True)
         zd.grad = None
-        loss = familywise_loss(zd, yd, reduction="mean")
-        loss.backward()
         if world > 1:
-            l2 = loss.detach().clone()
-            dist.all_reduce(l2)
-            loss = l2
-        lh[i:i + 1].copy_(loss.detach().reshape(1), non_blocking=True)
+            loss = sharded_familywise_loss(zd, yd, Bg)
+        else:
+            loss = familywise_loss(zd, yd, reduction="mean")
+        loss.backward()
+        lh[i:i + 1].copy_(loss.detach().reshape(1).float(), non_blocking=True)
 
     for i in range(min(2, a.warmup)):
         e2e_step(i)
     torch.cuda.synchronize(dev)
-    barrier()
-    ee0, ee1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ee0.record(stream)
-    for i in range(ne):
-        e2e_step(a.warmup + i)
-    ee1.record(stream)
-    torch.cuda.synchronize(dev)
-    barrier()
-    e_ms = ee0.elapsed_time(ee1)
-    t = torch.tensor([e_ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e_ms = float(t.item())
+
+    def e2e_loop():
+        for i in range(ne):
+            e2e_step(a.warmup + i)
+
+    e_ms = timed(e2e_loop)
     e2e = {"value": Bg * ne / (e_ms / 1e3), "unit": UNIT,
-           "h2d_bytes_per_step": int(zh.numel() * esize + yh.numel() * 8), "d2h_bytes_per_step": 4,
-           "ms_per_step": e_ms / ne, "api": "fwloss_b200.familywise_loss(mean).backward()"}
+           "h2d_bytes_per_step": int(Bg * C * esize + Bg * 8), "d2h_bytes_per_step": 4 * world,
+           "ms_per_step": e_ms / ne,
+           "api": ("fwloss_b200.distributed.sharded_familywise_loss(rows, labels, global_batch).backward()"
+                   if world > 1 else "fwloss_b200.familywise_loss(mean).backward()"),
+           "bytes": "summed over the ranks"}
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
@@ -535,29 +600,33 @@ def run_ours(a):
                    "sample": f"failed: {ex!r}"[:200]}
 
     if rank == 0:
-        launches_per_step = 2
+        launches_per_step = 2  # fused kernel + loss reduction (the NCCL all-reduce is NCCL's)
+        traffic = rows_traffic(profile_traffic(a.config if a.dtype == "f32" else f"{a.config}_{a.dtype}"), B,
+                               B_cfg)
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": ms / a.steps, "higher_is_better": True,
-            "scaling": "strong" if a.strong else "weak", "vs_baseline": None, "dtype": a.dtype,
+            "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": a.dtype,
             "data": "synthetic",
-            "config": dict(workload_desc(a.config, B, C, world, esize), global_batch=Bg,
-                           launch=("CUDA graph of the K timed steps" if use_graph and copies > 1 else
-                                   "CUDA-graph replay of each step" if use_graph else "eager")),
+            "config": bench_config(a.config, world, strong, esize),
+            "launch": launch_mode,
             "hbm_gbs": alg_bytes * a.steps / (ms / 1e3) / 1e9,
             "roofline": {"bound": "hbm", "kernel": ("fw_f64_rows_kernel" if esize == 8 else
                                                     "fw_stream_rows_kernel" if C > 2048 else "fw_warp_rows_kernel"),
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_kind": peak_kind,
-                         "traffic": rows_traffic(profile_traffic(a.config if a.dtype == "f32" else
-                                                                 f"{a.config}_{a.dtype}"), B, Bg if a.strong else B),
-                         "alg_bytes_per_launch": alg_bytes, "kernel_ms": k_ms},
+                         "peak_kind": peak_kind, "traffic": traffic,
+                         "alg_bytes_per_launch": alg_bytes, "kernel_ms": k_ms, "rows_per_launch": B},
+            "forward_only": fwd,
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": launches_per_step * a.steps,
             "clocks": clocks,
         }
+        if weak is not None:
+            line["weak"] = weak
         print(json.dumps(line), flush=True)
+    run_steps = g_steps = None  # graphs holding NCCL calls go before the process group
+    torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -46,6 +46,99 @@ def _worker(rank, world, port, B, C, out):
     dist.destroy_process_group()
 
 
+class _OracleExt:
+    """Stands in for the native module on CPU tensors (test only): the three
+    kernel calls the row-sharded autograd function makes, computed by the
+    oracle, so that the function's host logic (scale 1/B_global, loss
+    reduction, all-reduce, backward scaling) runs unchanged under gloo."""
+
+    def __init__(self):
+        from oracle import fw_oracle as O
+
+        self.O = O
+        self.calls = []
+
+    def fused_fwd_bwd(self, z, y, scale, status):
+        self.calls.append(("fused_fwd_bwd", scale))
+        s = self.O.solve(z.numpy(), y.numpy(), scale)
+        return (torch.from_numpy(s["grad"].astype(np.float32)), torch.from_numpy(s["H"].astype(np.float32)),
+                torch.from_numpy(s["loss"].astype(np.float32)), torch.from_numpy(s["kappa"].astype(np.int32)))
+
+    def forward_rows(self, z, y, status):
+        self.calls.append(("forward_rows",))
+        s = self.O.solve(z.numpy(), y.numpy(), 1.0)
+        return (torch.from_numpy(s["H"].astype(np.float32)), torch.from_numpy(s["loss"].astype(np.float32)),
+                torch.from_numpy(s["kappa"].astype(np.int32)))
+
+    def loss_reduce(self, losses, scale):
+        self.calls.append(("loss_reduce", scale))
+        return torch.tensor(float(losses.double().sum()) * scale, dtype=torch.float32)
+
+    def scale_grad(self, grad, grad_output, per_row, assumed):
+        self.calls.append(("scale_grad", per_row))
+        f = grad_output.double() / assumed
+        grad.mul_((f.reshape(-1, 1) if per_row else f.reshape(())).to(grad.dtype))
+
+
+def _worker_autograd(rank, world, port, B, C, out):
+    import sys
+
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    for p in (repo, os.path.join(repo, "fast-familywise-loss_b200")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    from fwloss_b200 import distributed as D
+
+    fake = _OracleExt()
+    D.ext = lambda: fake               # the kernels, on the CPU (test only)
+    D._check_inputs = lambda z, y: None  # the product path requires CUDA tensors
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    rng = np.random.default_rng(7)
+    z = rng.standard_normal((B, C)).astype(np.float32)
+    y = rng.integers(0, C, B)
+    a, b = D.shard_rows(B, rank, world)
+    zl = torch.from_numpy(z[a:b].copy()).requires_grad_(True)
+    yl = torch.from_numpy(y[a:b].copy())
+    loss = D.sharded_familywise_loss(zl, yl, B)
+    (loss * 3.0).backward()
+    with torch.no_grad():
+        nograd = D.sharded_familywise_loss(zl, yl, B)
+    out[rank] = (float(loss), zl.grad.numpy().copy(), a, b, float(nograd), list(fake.calls))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_autograd_function_host_logic(world):
+    """sharded_familywise_loss forward/backward under gloo with the kernel
+    calls stubbed: every rank returns the global mean loss, its rows of the
+    global gradient times the upstream factor, the fused kernel runs with the
+    global scale 1/B, and the no-grad call takes the forward-only kernel."""
+    B, C = 29, 150
+    mgr = mp.get_context("spawn").Manager()
+    out = mgr.dict()
+    mp.start_processes(_worker_autograd, args=(world, _free_port(), B, C, out), nprocs=world, join=True,
+                       start_method="spawn")
+    from oracle import fw_oracle as O
+
+    rng = np.random.default_rng(7)
+    z = rng.standard_normal((B, C)).astype(np.float32)
+    y = rng.integers(0, C, B)
+    full = O.solve(z, y, 1.0 / B)
+    mean = full["loss"].mean()
+    for r in range(world):
+        loss, g, a, b, nograd, calls = out[r]
+        np.testing.assert_allclose(loss, mean, rtol=1e-6)
+        np.testing.assert_allclose(nograd, mean, rtol=1e-6)
+        np.testing.assert_allclose(g, 3.0 * full["grad"][a:b], rtol=1e-6, atol=1e-9)
+        assert calls[0] == ("fused_fwd_bwd", 1.0 / B) and ("loss_reduce", 1.0 / B) in calls
+        assert ("scale_grad", False) in calls and ("forward_rows",) in calls
+    assert sorted(out[r][2] for r in range(world)) == [out[r][2] for r in range(world)]
+    assert sum(out[r][3] - out[r][2] for r in range(world)) == B
+
+
 @pytest.mark.parametrize("world", [2, 4])
 def test_sharded_loss_and_grad_equal_global(world):
     B, C = 37, 300
