@@ -22,9 +22,10 @@
                                      the benchmark times next to ours and a
                                      parity check of kappa.
 
-The reference build needs the reference checkout (environment variable
-FW_REF_PATH, or the default REF_PATH below); where it is absent (e.g. on a GPU
-box) the prebuilt files travel with the tree and this step is skipped.
+The reference build needs the reference checkout: the directory named by the
+environment variable FW_REF_PATH, or else a checkout named `reference` beside
+this repository (REF_PATH below); where it is absent (e.g. on a GPU box) the
+prebuilt files travel with the tree and this step is skipped.
 """
 import os
 import subprocess
@@ -35,7 +36,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 BUILD = os.path.join(HERE, "_build")
 REF_OUT = os.path.join(HERE, "_ref")
 ORACLE_SO = os.path.join(BUILD, "libfw_oracle.so")
-REF_PATH = os.environ.get("FW_REF_PATH", "/root/reference")
+REF_PATH = os.environ.get("FW_REF_PATH") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
 REF_SRC = os.path.join(REF_PATH, "src", "cpu", "fw_cpu.cpp")
 ISAS = {"avx512": "-march=x86-64-v4", "avx2": "-march=x86-64-v3"}
 SUFFIX = sysconfig.get_config_var("EXT_SUFFIX")

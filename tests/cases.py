@@ -28,6 +28,29 @@ def golden_inputs_match(golden, name, z, y):
     return key in golden.files and str(golden[key]) == input_sha256(z, y)
 
 
+def committed_config_inputs(name):
+    """(z [n, C] float32, y [n] int64, rows of the fixture case) of a reduced
+    benchmark configuration, read from tests/golden/config_inputs.npz (its
+    first n rows, stored by tests/golden/gen_golden.py --config-inputs)."""
+    import os
+
+    d = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "config_inputs.npz"))
+    return d[f"{name}/z"], d[f"{name}/y"], int(d[f"{name}/case_rows"])
+
+
+def golden_first_rows(golden, name, n, C):
+    """The golden outputs of case `name` for its first n rows: the reference
+    CPU kernel's kappa, loss and dense gradient, and reference_impl's fp32
+    kappa, H and loss."""
+    out = {k: golden[f"{name}/{k}"][:n] for k in ("kappa_cpu", "loss_cpu", "kappa_ref32", "H_ref32", "loss_ref32")}
+    r, c, v = (golden[f"{name}/grad_cpu_{s}"] for s in "rcv")
+    keep = r < n
+    g = np.zeros((n, C), np.float32)
+    g[r[keep], c[keep]] = v[keep]
+    out["grad_cpu"] = g
+    return out
+
+
 def _rng(seed):
     return np.random.default_rng(seed)
 

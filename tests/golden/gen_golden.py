@@ -1,8 +1,8 @@
 """Writes the golden fixtures of tests/golden/ from the REFERENCE itself.
 
-Run in a container that has the reference checkout (environment variable
-FW_REF_PATH, or the default REF below) and the reference CPU extension built
-by oracle/build.py:
+Run in a container that has the reference checkout (the directory named by the
+environment variable FW_REF_PATH, or else a checkout named `reference` beside
+this repository) and the reference CPU extension built by oracle/build.py:
 
     python tests/golden/gen_golden.py
 
@@ -22,6 +22,10 @@ its scalar kernels instead of the AVX2/AVX-512 ones):
                          reference_impl.FWLoss on float64 tensors and the
                          CPU extension's float64 branch (fw_cpu.cpp:698-704);
                          gradients in float64.
+  config_inputs.npz      the inputs of the reduced benchmark configurations
+                         (first rows of each; `--config-inputs` rewrites only
+                         this file), so that their reference pin needs no
+                         regeneration on the testing host.
   kat_kbar.json          the known answers the reference ships: the `kbar`
                          (mean kappa over 32 rows) of every (distribution,
                          sigma, K) in benchmarks/cpu_benchmarks/results/*.json,
@@ -40,7 +44,7 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 sys.path.insert(0, os.path.join(REPO, "tests"))
 sys.path.insert(0, os.path.join(REPO, "fast-familywise-loss_b200"))
-REF = os.environ.get("FW_REF_PATH", "/root/reference")
+REF = os.environ.get("FW_REF_PATH") or os.path.join(os.path.dirname(REPO), "reference")
 sys.path.insert(0, REF)
 
 import torch  # noqa: E402
@@ -130,7 +134,36 @@ def kat():
     return out
 
 
+# Rows of each reduced configuration whose inputs are stored in
+# config_inputs.npz (the first rows of the fixture cases above; fewer rows
+# where the full case would be large).
+STORED_ROWS = {"cfg0": 256, "cfg1": 512, "cfg2": 16, "cfg3": 2048, "cfg4": 4}
+
+
+def write_config_inputs():
+    """config_inputs.npz: the inputs of the reduced benchmark configurations
+    (their first STORED_ROWS rows), so that the golden comparison of those
+    cases does not depend on the host regenerating them with torch's CPU
+    generator.  Checked against the fingerprint the fixtures recorded for the
+    whole case."""
+    golden = np.load(os.path.join(HERE, "reference_outputs.npz"))
+    store = {}
+    for name, rows in CONFIG_ROWS.items():
+        z, y = workloads.make(name, rows=rows)
+        z, y = z.numpy(), y.numpy()
+        assert str(golden[f"{name}/input_sha256"]) == str(input_sha256(z, y)), \
+            f"{name}: this host regenerates other inputs than the fixtures were made from"
+        n = STORED_ROWS[name]
+        store[f"{name}/z"] = np.ascontiguousarray(z[:n])
+        store[f"{name}/y"] = np.ascontiguousarray(y[:n])
+        store[f"{name}/case_rows"] = np.int64(rows)
+    np.savez_compressed(os.path.join(HERE, "config_inputs.npz"), **store)
+
+
 def main():
+    if "--config-inputs" in sys.argv:  # only the stored inputs (fixtures unchanged)
+        write_config_inputs()
+        return
     store = {}
     for name, gen in all_cases():
         z, y = gen()
