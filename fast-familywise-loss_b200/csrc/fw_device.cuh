@@ -141,6 +141,7 @@ struct RowArgs {
   int32_t* sup_cols;     // kOutGrad, optional: [B, sup_k] support columns (the first
                          // min(kappa, sup_k)); -1 in the first slot when not listed
   int sup_k;
+  int wait_prior;        // streaming tier: wait for the previous grid before exiting
 };
 
 // max() that returns NaN when either input is NaN (fmaxf would drop it).
@@ -210,15 +211,11 @@ __device__ __forceinline__ double group_sum(double v, unsigned gmask) {
   return v;
 }
 
+// One redux.sync over the group's lanes (each group of a warp names its own
+// member mask; the lanes of one mask wait only for each other).
 template <int G>
 __device__ __forceinline__ int group_sum(int v, unsigned gmask) {
-  if constexpr (G == 32) {
-    return __reduce_add_sync(gmask, v);
-  } else {
-#pragma unroll
-    for (int o = G / 2; o > 0; o >>= 1) v += __shfl_xor_sync(gmask, v, o);
-    return v;
-  }
+  return __reduce_add_sync(gmask, v);
 }
 
 template <int G>
@@ -259,7 +256,9 @@ __device__ __forceinline__ float threshold_fp32(float M, double tau) {
 // is deterministic.  All G lanes of the group must call it with the same
 // arguments; all return the same (tau, kappa).
 // CAP > 0 bounds n (n <= CAP) and turns the per-lane loop into CAP/G
-// predicated steps; CAP == 0 means any n.
+// predicated steps; CAP == 0 means any n.  The kept count is reduced first
+// (one redux.sync); the fp64 sum only when the set changed, so the final,
+// confirming pass costs no fp64 reduction.
 template <int G, int CAP = 0>
 __device__ __forceinline__ void michelot_list(const float* L, int n, float M, int li,
                                               unsigned gmask, double& tau, int& kappa) {
@@ -284,11 +283,70 @@ __device__ __forceinline__ void michelot_list(const float* L, int n, float M, in
       }
     }
     c = group_sum<G>(c, gmask);
-    s = group_sum<G>(s, gmask);
     if (c == prev) break;
+    s = group_sum<G>(s, gmask);
     prev = c;
     t = (s - 1.0) / (double)c;
     Ht = threshold_fp32(M, t);
+  }
+  tau = t;
+  kappa = prev;
+}
+
+// Michelot's fixed point with at most one candidate per lane: x is this
+// lane's candidate (-inf when it has none), n >= 1 the number of candidates
+// in the group, all of them above t0.  Counts are one ballot; the fp64 sum a
+// butterfly, taken only while the kept set changes.  Same sets, threshold
+// predicate and result as michelot_list on the same candidates.
+template <int G>
+__device__ __forceinline__ void michelot_lane(float x, int n, float M, unsigned gmask, double& tau,
+                                              int& kappa) {
+  const double d = (double)x - (double)M;  // used only where x is kept
+  double s = group_sum<G>(x > -CUDART_INF_F ? d : 0.0, gmask);
+  int cnt = n;
+  double t = (s - 1.0) / (double)cnt;
+  for (int it = 0; it < n; ++it) {
+    const float Ht = threshold_fp32(M, t);
+    const bool keep = x > Ht;
+    const int c = __popc(__ballot_sync(gmask, keep) & gmask);
+    if (c == cnt) break;
+    s = group_sum<G>(keep ? d : 0.0, gmask);
+    cnt = c;
+    t = (s - 1.0) / (double)cnt;
+  }
+  tau = t;
+  kappa = cnt;
+}
+
+// Michelot's fixed point on a row held in registers (NV values per lane, G
+// lanes), starting from the superset {v > t0}.  Each pass counts and sums the
+// kept values; the count is reduced first (one redux.sync) and the fp64 sum
+// only while the kept set changes.  A set of one element is the maximum
+// alone: tau = -1 exactly, no further pass.  The threshold is never below t0,
+// so the sets are nested and at most (candidates + 1) passes run.
+template <int G, int NV>
+__device__ __forceinline__ void michelot_regs(const float (&v)[NV], float M, float t0, unsigned gmask,
+                                              double& tau, int& kappa) {
+  const double Md = (double)M;
+  double t = -CUDART_INF;
+  float Ht = t0;
+  int prev = -1;
+  for (int it = 0; it <= G * NV; ++it) {
+    double s = 0.0;
+    int c = 0;
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+      if (v[k] > Ht) { s += (double)v[k] - Md; ++c; }
+    c = group_sum<G>(c, gmask);
+    if (c == prev) break;
+    prev = c;
+    if (c == 1) {  // the maximum alone: h* = M - 1
+      t = -1.0;
+      break;
+    }
+    s = group_sum<G>(s, gmask);
+    t = (s - 1.0) / (double)c;
+    Ht = fmaxf(threshold_fp32(M, t), t0);
   }
   tau = t;
   kappa = prev;

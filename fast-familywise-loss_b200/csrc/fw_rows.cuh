@@ -8,7 +8,7 @@
 //                      (fw_warp_tier.cuh).
 //   C  > 2048          CTA per row (CS = 1) or a cluster of CS = 2/4/8 CTAs per
 //                      row when there are too few rows to fill the GPU
-//                      (fw_stream_tier.cuh).
+//                      (fw_stream_tier.cuh; launch plan: dispatch_stream).
 // 128-bit loads/stores are used when every row starts on a 16-byte boundary
 // (base pointers 16-byte aligned and ld % 4 == 0); otherwise the same kernels
 // run with coalesced 32-bit accesses.
@@ -31,20 +31,21 @@ cudaError_t launch_warp_tier(const RowArgs& a, cudaStream_t st) {
   const bool fullv = VEC && (a.C % Elem<T>::kEPS == 0);
   auto k = fullv ? fw_warp_rows_kernel<T, G, NS, VEC, OUT, VEC>
                  : fw_warp_rows_kernel<T, G, NS, VEC, OUT, false>;
+  constexpr int threads = warp_tier_threads<NS * Elem<T>::kEPS>();
   static std::atomic<int> occ[2] = {};  // resident CTAs per SM of the two instances
   int o = occ[fullv ? 1 : 0].load(std::memory_order_relaxed);
   if (o == 0) {
     int r = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, k, kWarpTierThreads, 0) != cudaSuccess || r < 1)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, k, threads, 0) != cudaSuccess || r < 1)
       r = 1;
     o = r;
     occ[fullv ? 1 : 0].store(o, std::memory_order_relaxed);
   }
-  const int64_t rows_per_block = (int64_t)kWarpTierWarps * (32 / G);
+  const int64_t rows_per_block = (int64_t)(threads / 32) * (32 / G);
   const int64_t need = (a.B + rows_per_block - 1) / rows_per_block;
   const int64_t cap = (int64_t)sm_count() * o;
   const int grid = (int)(need < cap ? need : cap);
-  return launch(k, dim3(grid), dim3(kWarpTierThreads), 1, st, a);
+  return launch(k, dim3(grid), dim3(threads), 1, st, a);
 }
 
 // Lanes per row G and register values per lane NV by class count:
@@ -62,32 +63,97 @@ cudaError_t dispatch_warp(const RowArgs& a, cudaStream_t st) {
 }
 
 // ----------------------------------------------------------- stream tier
-template <class T, int CS, bool VEC, int OUT, bool DEEP = false>
-cudaError_t launch_stream_tier(const RowArgs& a, cudaStream_t st) {
-  auto k = fw_stream_rows_kernel<T, CS, VEC, OUT, DEEP>;
-  const int64_t grid = a.B * CS;
-  return launch(k, dim3((unsigned)grid), dim3(kST), CS, st, a);
+// after_prior: launched as a programmatic dependent of the previous kernel on
+// the stream (its CTAs may start while that kernel's last CTAs run) and
+// waiting for that kernel before exiting (RowArgs::wait_prior).
+template <class T, int CS, bool VEC, int OUT, int SHAPE = kShapeWide>
+cudaError_t launch_stream_tier(const RowArgs& a, cudaStream_t st, bool after_prior = false) {
+  RowArgs b = a;
+  b.wait_prior = after_prior ? 1 : 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(a.B * CS));
+  cfg.blockDim = dim3(stream_threads<SHAPE>());
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (CS > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = CS;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (after_prior) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, fw_stream_rows_kernel<T, CS, VEC, OUT, SHAPE>, b);
 }
 
-// Cluster size: the smallest CS in {1, 2, 4, 8} giving at least 4 CTAs per SM,
-// while every CTA keeps a segment of at least 4096 columns.
-inline int choose_cluster(int64_t B, int64_t C) {
-  const int64_t want = (int64_t)sm_count() * 4;
+// The arguments for rows [r0, r0 + n) of a (every per-row pointer advanced).
+template <class T>
+RowArgs rows_from(const RowArgs& a, int64_t r0, int64_t n) {
+  RowArgs b = a;
+  b.B = n;
+  b.z = static_cast<const T*>(a.z) + r0 * a.ld;
+  if (a.y) b.y = a.y + r0;
+  if (a.grad) b.grad = static_cast<T*>(a.grad) + r0 * a.ld;
+  if (a.mask) b.mask = a.mask + r0 * a.C;
+  if (a.cand_val) b.cand_val = a.cand_val + r0 * a.C;
+  if (a.cand_idx) b.cand_idx = a.cand_idx + r0 * a.C;
+  if (a.cand_count) b.cand_count = a.cand_count + r0;
+  if (a.H) b.H = a.H + r0;
+  if (a.loss) b.loss = a.loss + r0;
+  if (a.kappa) b.kappa = a.kappa + r0;
+  if (a.shard_sum) b.shard_sum = a.shard_sum + r0 * (int64_t)(kShardHeader + a.shard_k);
+  if (a.shard_idx) b.shard_idx = a.shard_idx + r0 * (int64_t)a.shard_k;
+  if (a.sup_cols) b.sup_cols = a.sup_cols + r0 * (int64_t)a.sup_k;
+  return b;
+}
+
+// Cluster size for few rows: the largest CS in {1, 2, 4, 8} whose CTAs
+// (rows x CS) fit in `slots`, every CTA keeping >= 4096 columns.
+inline int fit_cluster(int64_t rows, int64_t C, int64_t slots) {
   int cs = 1;
-  while (cs < 8 && B * cs < want && C / (cs * 2) >= 4096) cs *= 2;
+  while (cs < 8 && rows * cs * 2 <= slots && C / (cs * 2) >= 4096) cs *= 2;
   return cs;
 }
 
 template <class T, bool VEC, int OUT>
-cudaError_t dispatch_stream(const RowArgs& a, cudaStream_t st) {
-  switch (choose_cluster(a.B, a.C)) {
-    case 8:  // at most two CTAs per SM: the instance with deeper load pipelining
-      return (a.B * 8 <= 2 * (int64_t)sm_count()) ? launch_stream_tier<T, 8, VEC, OUT, true>(a, st)
-                                                  : launch_stream_tier<T, 8, VEC, OUT>(a, st);
-    case 4: return launch_stream_tier<T, 4, VEC, OUT>(a, st);
-    case 2: return launch_stream_tier<T, 2, VEC, OUT>(a, st);
-    default: return launch_stream_tier<T, 1, VEC, OUT>(a, st);
+cudaError_t launch_deep(const RowArgs& a, cudaStream_t st, int cs, bool after_prior) {
+  switch (cs) {
+    case 8: return launch_stream_tier<T, 8, VEC, OUT, kShapeDeep>(a, st, after_prior);
+    case 4: return launch_stream_tier<T, 4, VEC, OUT, kShapeDeep>(a, st, after_prior);
+    case 2: return launch_stream_tier<T, 2, VEC, OUT, kShapeDeep>(a, st, after_prior);
+    default: return launch_stream_tier<T, 1, VEC, OUT, kShapeDeep>(a, st, after_prior);
   }
+}
+
+// Launch plan for B rows (one CTA per row; resident slots: 5 CTAs per SM of
+// the wide shape, 2 of the deep one):
+//  * B <= deep slots: the deep shape, with clusters of CS CTAs per row when
+//    rows x CS still fits one deep wave (e.g. 32 rows x 1e6 columns: CS 8);
+//  * otherwise one CTA per row in the wide shape; when that leaves a last
+//    wave of at most (deep slots) rows, those rows go to a second launch in
+//    the deep shape (clustered as above), started as a programmatic
+//    dependent so that it runs under the first launch's last CTAs: a short
+//    last wave of the wide shape is latency-bound (B200, C = 32000 fp32:
+//    768 rows took 44.0 us against 22.6 us for 512 rows, 1024 rows 51.0 us).
+template <class T, bool VEC, int OUT>
+cudaError_t dispatch_stream(const RowArgs& a, cudaStream_t st) {
+  const int64_t sms = sm_count();
+  const int64_t deep = sms * stream_min_blocks<kShapeDeep>();
+  const int64_t wide = sms * stream_min_blocks<kShapeWide>();
+  if (a.B <= deep) return launch_deep<T, VEC, OUT>(a, st, fit_cluster(a.B, a.C, deep), false);
+  const int64_t tail = a.B % wide;
+  if (a.B <= wide || tail == 0 || tail > deep) return launch_stream_tier<T, 1, VEC, OUT>(a, st);
+  const int64_t head = a.B - tail;
+  const cudaError_t e = launch_stream_tier<T, 1, VEC, OUT>(rows_from<T>(a, 0, head), st);
+  if (e != cudaSuccess) return e;
+  return launch_deep<T, VEC, OUT>(rows_from<T>(a, head, tail), st, fit_cluster(tail, a.C, deep), true);
 }
 
 }  // namespace

@@ -49,31 +49,48 @@
 
 namespace fwb200 {
 
-constexpr int kST = 256;              // threads per CTA
-constexpr int kSW = kST / 32;         // warps per CTA
+constexpr int kST = 256;              // threads per CTA (wide and deep shapes; the most)
+constexpr int kSW = kST / 32;         // warps per CTA (the most: shared-memory sizing)
 constexpr int kStreamListCap = 128;   // candidates per warp list
 constexpr int kSolveCap = 1024;       // gathered candidates per row
 constexpr int kStreamItems = 4;       // 16-byte loads per thread per streaming step (VEC)
 constexpr int kStreamScalars = 16;    // scalar loads per thread per streaming step (!VEC)
 
-// Loads per thread per streaming step: four 16-byte loads in flight for every
-// element type (16 fp32 or 32 bf16/fp16 values), 16 scalars without VEC.
-// DEEP instances (a grid of at most two CTAs per SM: very few rows, each on a
-// cluster of 8 CTAs) keep eight 16-byte loads in flight per thread instead,
-// since few CTAs share an SM (B200, B = 32 x C = 1e6 fp32: 93.2 -> 83.1 us).
-template <bool VEC, bool DEEP = false>
-__host__ __device__ constexpr int stream_ipt() {
-  return VEC ? (DEEP ? 2 * kStreamItems : kStreamItems) : kStreamScalars;
+// Launch shapes of the streaming kernel (16-byte loads in flight per thread,
+// resident CTAs per SM the register budget is sized for), 256 threads each:
+//   kShapeWide  4 loads, 5 CTAs per SM (<= 51 registers; 16-bit rows stream
+//               in half the time of fp32 ones, so more CTAs are needed to
+//               cover each row's exchange/solve/patch phase: B200, cfg2
+//               shape, bf16 99.1 -> 97.0 us, fp32 unchanged, six CTAs slower);
+//   kShapeDeep  8 loads, 2 CTAs per SM: grids of at most two CTAs per SM
+//               (very few rows, or the rows left over after whole waves),
+//               where few CTAs share an SM and each has to keep more bytes in
+//               flight (B200, B = 32 x C = 1e6 fp32 on clusters of 8:
+//               93.2 -> 83.1 us).
+// Without 16-byte loads (unaligned rows) both issue 16 scalar loads per
+// thread per step.
+enum StreamShape : int { kShapeWide = 0, kShapeDeep = 2 };
+
+template <int SHAPE>
+__host__ __device__ constexpr int stream_threads() {
+  return kST;
 }
 
-// Resident CTAs per SM the register budget is sized for: five (<= 51
-// registers; 16-bit rows stream in half the time of fp32 ones, so more CTAs
-// are needed to cover each row's exchange/solve/patch phase: B200, cfg2
-// shape, bf16 99.1 -> 97.0 us, fp32 unchanged, six CTAs slower); two for the
-// DEEP instances, whose threads hold twice the values.
-template <bool DEEP>
+template <bool VEC, int SHAPE = kShapeWide>
+__host__ __device__ constexpr int stream_ipt() {
+  return VEC ? (SHAPE == kShapeWide ? kStreamItems : 2 * kStreamItems) : kStreamScalars;
+}
+
+template <int SHAPE>
 __host__ __device__ constexpr int stream_min_blocks() {
-  return DEEP ? 2 : 5;
+  return SHAPE == kShapeWide ? 5 : 2;
+}
+
+// Waits until the grid launched before this one on the stream has completed
+// and its writes are visible (griddepcontrol.wait); returns at once for a
+// launch that is not a programmatic dependent.
+__device__ __forceinline__ void wait_prior_grid() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 struct __align__(16) StreamShared {
@@ -194,18 +211,18 @@ __device__ __forceinline__ Segment row_segment(int64_t C, int rank) {
 // Calls f(value, column) for every element of this thread's share of the
 // segment, in the fixed order used by all passes (loads are issued kStreamU
 // 16-byte items ahead).  f must be thread-local work only.
-template <class T, int CS, bool VEC, class F>
+template <class T, int CS, bool VEC, int NT, class F>
 __device__ __forceinline__ void for_each_element(const T* zr, int64_t C,
                                                  int rank, F&& f) {
   constexpr int EPS = Elem<T>::kEPS;
   const Segment g = row_segment<CS, VEC, EPS>(C, rank);
   constexpr int W = VEC ? EPS : 1;
   constexpr int IPT = stream_ipt<VEC>();
-  for (int64_t base = g.i0; base < g.i1; base += (int64_t)kST * IPT) {
+  for (int64_t base = g.i0; base < g.i1; base += (int64_t)NT * IPT) {
     float v[IPT * W];
 #pragma unroll
     for (int u = 0; u < IPT; ++u) {
-      const int64_t it = base + (int64_t)u * kST + threadIdx.x;
+      const int64_t it = base + (int64_t)u * NT + threadIdx.x;
       if (VEC) {
         if (it < g.i1) {
           unpack16<T>(ld_stream16(zr + W * it), &v[W * u]);
@@ -219,7 +236,7 @@ __device__ __forceinline__ void for_each_element(const T* zr, int64_t C,
     }
 #pragma unroll
     for (int u = 0; u < IPT; ++u) {
-      const int64_t it = base + (int64_t)u * kST + threadIdx.x;
+      const int64_t it = base + (int64_t)u * NT + threadIdx.x;
       if (it < g.i1) {
 #pragma unroll
         for (int j = 0; j < W; ++j) f(v[u * W + j], (int)(it * W + j));
@@ -232,15 +249,14 @@ __device__ __forceinline__ void for_each_element(const T* zr, int64_t C,
   }
 }
 
-template <class T, int CS, bool VEC, int OUT, bool DEEP = false>
-__global__ void __launch_bounds__(kST, stream_min_blocks<DEEP>())
-    fw_stream_rows_kernel(RowArgs a) {
-  allow_dependent_launch();
+template <class T, int CS, bool VEC, int OUT, int SHAPE>
+__device__ __forceinline__ void stream_rows_body(const RowArgs& a, StreamShared& s) {
+  constexpr int NT = stream_threads<SHAPE>();  // threads per CTA
+  constexpr int NW = NT / 32;                  // warps per CTA
   static_assert(OUT == kOutGrad || OUT == kOutNone || sizeof(T) == 4,
                 "mask/candidate/shard outputs are fp32-only");
   constexpr bool kZeroFill = (OUT == kOutGrad || OUT == kOutShard);
   constexpr int EPS = Elem<T>::kEPS;
-  __shared__ StreamShared s;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int w = tid >> 5;
@@ -262,7 +278,7 @@ __global__ void __launch_bounds__(kST, stream_min_blocks<DEEP>())
 
   // ---------------------------------------------------------------- stream
   constexpr int W = VEC ? EPS : 1;
-  constexpr int IPT = stream_ipt<VEC, DEEP>();
+  constexpr int IPT = stream_ipt<VEC, SHAPE>();
   const Segment g = row_segment<CS, VEC, EPS>(C, rank);
   float run = -CUDART_INF_F;
   int wcnt = 0;
@@ -273,11 +289,11 @@ __global__ void __launch_bounds__(kST, stream_min_blocks<DEEP>())
   T* gr = (kZeroFill && a.grad) ? static_cast<T*>(a.grad) + row * a.ld : nullptr;
   uint8_t* mr = (OUT == kOutMask) ? a.mask + row * C : nullptr;
 
-  for (int64_t base = g.i0; base < g.i1; base += (int64_t)kST * IPT) {
+  for (int64_t base = g.i0; base < g.i1; base += (int64_t)NT * IPT) {
     float v[IPT * W];
 #pragma unroll
     for (int u = 0; u < IPT; ++u) {
-      const int64_t it = base + (int64_t)u * kST + tid;
+      const int64_t it = base + (int64_t)u * NT + tid;
       if (VEC) {
         if (it < g.i1) {
           unpack16<T>(ld_stream16(zr + W * it), &v[W * u]);
@@ -291,7 +307,7 @@ __global__ void __launch_bounds__(kST, stream_min_blocks<DEEP>())
     }
 #pragma unroll
     for (int u = 0; u < IPT; ++u) {
-      const int64_t it = base + (int64_t)u * kST + tid;
+      const int64_t it = base + (int64_t)u * NT + tid;
       if (it < g.i1) {
         if (kZeroFill && (OUT == kOutGrad || gr != nullptr)) {
           if (VEC)
@@ -321,7 +337,7 @@ __global__ void __launch_bounds__(kST, stream_min_blocks<DEEP>())
     if (__any_sync(kFull, anyc)) {
 #pragma unroll
       for (int u = 0; u < IPT; ++u) {
-        const int64_t it = base + (int64_t)u * kST + tid;
+        const int64_t it = base + (int64_t)u * NT + tid;
 #pragma unroll
         for (int j = 0; j < W; ++j)
           list_append(lz, li, wcnt, ovf, v[u * W + j], (int)(it * W + j),
@@ -358,13 +374,13 @@ __global__ void __launch_bounds__(kST, stream_min_blocks<DEEP>())
     // row needs no second and third barrier.
     M = -CUDART_INF_F;
 #pragma unroll
-    for (int k = 0; k < kSW; ++k) M = max_nan(M, s.wmax[k]);
+    for (int k = 0; k < NW; ++k) M = max_nan(M, s.wmax[k]);
     row_flags = s.flags;
   } else {
     if (tid == 0) {
       float cm = -CUDART_INF_F;
 #pragma unroll
-      for (int k = 0; k < kSW; ++k) cm = max_nan(cm, s.wmax[k]);
+      for (int k = 0; k < NW; ++k) cm = max_nan(cm, s.wmax[k]);
       s.cta_max = cm;
     }
     row_barrier<CS>();
@@ -397,7 +413,7 @@ __global__ void __launch_bounds__(kST, stream_min_blocks<DEEP>())
   if (!isfinite(M)) {
     const bool isn = (M != M);
     int best = INT_MAX;
-    for_each_element<T, CS, VEC>(zr, C, rank, [&](float x, int c) {
+    for_each_element<T, CS, VEC, NT>(zr, C, rank, [&](float x, int c) {
       if (isn ? (x != x) : (x == M)) best = min(best, c);
     });
     best = (int)__reduce_min_sync(kFull, (unsigned)best);
@@ -447,23 +463,23 @@ __global__ void __launch_bounds__(kST, stream_min_blocks<DEEP>())
   // ---------------------------------------------------------------- gather
   const bool lists_ok = !(row_flags & 1);  // no warp list overflowed
   if constexpr (CS == 1) {
-    // One CTA: the warp lists hold at most kSW * kStreamListCap <= kSolveCap
+    // One CTA: the warp lists hold at most NW * kStreamListCap <= kSolveCap
     // candidates, so the gathered list cannot overflow and warp 0 alone
     // finishes the row; the zero stores of the other warps precede the
     // barrier above, which orders them before warp 0's patch.
-    static_assert(kSW * kStreamListCap <= kSolveCap, "one CTA's lists must fit the solve list");
+    static_assert(NW * kStreamListCap <= kSolveCap, "one CTA's lists must fit the solve list");
     if (lists_ok && w != 0) return;
   }
   if constexpr (CS > 1) {
-    // The leader CTA's warps gather the CS * kSW lists in parallel (their
+    // The leader CTA's warps gather the CS * NW lists in parallel (their
     // entries sit in other CTAs' shared memory): kept counts per list, their
     // offsets in the fixed list order (rank-major, then warp), then the
     // copies.  Same list, in the same order, as one warp walking the lists.
     if (lists_ok && leader) {
-      constexpr int NL = CS * kSW;
-      for (int L = w; L < NL; L += kSW) {
-        const StreamShared* rs = cta_smem<CS>(&s, L / kSW);
-        const int ww = L % kSW;
+      constexpr int NL = CS * NW;
+      for (int L = w; L < NL; L += NW) {
+        const StreamShared* rs = cta_smem<CS>(&s, L / NW);
+        const int ww = L % NW;
         const int cnt = rs->wcnt[ww];
         int kept = 0;
         for (int k0 = 0; k0 < cnt; k0 += 32) {
@@ -490,9 +506,9 @@ __global__ void __launch_bounds__(kST, stream_min_blocks<DEEP>())
       }
       __syncthreads();
       if (!s.go_dense) {
-        for (int L = w; L < NL; L += kSW) {
-          const StreamShared* rs = cta_smem<CS>(&s, L / kSW);
-          const int ww = L % kSW;
+        for (int L = w; L < NL; L += NW) {
+          const StreamShared* rs = cta_smem<CS>(&s, L / NW);
+          const int ww = L % NW;
           const int cnt = rs->wcnt[ww];
           int pos0 = s.goff[L];
           for (int k0 = 0; k0 < cnt; k0 += 32) {
@@ -520,7 +536,7 @@ __global__ void __launch_bounds__(kST, stream_min_blocks<DEEP>())
     bool full = false;
     for (int r = 0; r < CS && !full; ++r) {
       const StreamShared* rs = cta_smem<CS>(&s, r);
-      for (int ww = 0; ww < kSW && !full; ++ww) {
+      for (int ww = 0; ww < NW && !full; ++ww) {
         const int cnt = rs->wcnt[ww];
         for (int k0 = 0; k0 < cnt; k0 += 32) {
           const int k = k0 + lane;
@@ -655,12 +671,12 @@ __global__ void __launch_bounds__(kST, stream_min_blocks<DEEP>())
   unsigned long long cut = 1ull << 32;  // selected <=> key >= cut (and z > t0)
   const double t0d = (double)t0 - Md;
   for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int b = tid; b < 256; b += kST) {
+    for (int b = tid; b < 256; b += NT) {
       s.hc[b] = 0;
       s.hs[b] = 0.0;
     }
     __syncthreads();
-    for_each_element<T, CS, VEC>(zr, C, rank, [&](float x, int) {
+    for_each_element<T, CS, VEC, NT>(zr, C, rank, [&](float x, int) {
       if (x > t0) {
         const uint32_t k = sort_key(x);
         if ((k & pmask) == prefix) {
@@ -673,7 +689,7 @@ __global__ void __launch_bounds__(kST, stream_min_blocks<DEEP>())
     row_barrier<CS>();
     if (leader) {
       if (CS > 1) {
-        for (int b = tid; b < 256; b += kST) {
+        for (int b = tid; b < 256; b += NT) {
           int c = s.hc[b];
           double sm = s.hs[b];
           for (int r = 1; r < CS; ++r) {
@@ -744,7 +760,7 @@ __global__ void __launch_bounds__(kST, stream_min_blocks<DEEP>())
     return x > t0 && (unsigned long long)sort_key(x) >= cut;
   };
   if (OUT == kOutGrad) {
-    for_each_element<T, CS, VEC>(zr, C, rank, [&](float x, int c) {
+    for_each_element<T, CS, VEC, NT>(zr, C, rank, [&](float x, int c) {
       float gv = sel_of(x) ? inv : 0.0f;
       if (c == yc) gv -= a.scale;
       st_elem(gr + c, gv);
@@ -752,13 +768,13 @@ __global__ void __launch_bounds__(kST, stream_min_blocks<DEEP>())
     // dense rows do not list their support (consumers fall back to the row)
     if (a.sup_cols && leader && tid == 0) a.sup_cols[row * (int64_t)a.sup_k] = -1;
   } else if (OUT == kOutMask) {
-    for_each_element<T, CS, VEC>(zr, C, rank, [&](float x, int c) { mr[c] = sel_of(x) ? 1 : 0; });
+    for_each_element<T, CS, VEC, NT>(zr, C, rank, [&](float x, int c) { mr[c] = sel_of(x) ? 1 : 0; });
   } else if (OUT == kOutShard) {
     int* pos_ctr = &cta_smem<CS>(&s, 0)->cand_pos;
     const int K = a.shard_k;
     int32_t* rec = a.shard_sum + row * (int64_t)(kShardHeader + K);
     int32_t* ridx = a.shard_idx + row * (int64_t)K;
-    for_each_element<T, CS, VEC>(zr, C, rank, [&](float x, int c) {
+    for_each_element<T, CS, VEC, NT>(zr, C, rank, [&](float x, int c) {
       if (sel_of(x)) {
         const int p = atomicAdd(pos_ctr, 1);
         if (p < K) {
@@ -781,7 +797,7 @@ __global__ void __launch_bounds__(kST, stream_min_blocks<DEEP>())
     int* pos_ctr = &cta_smem<CS>(&s, 0)->cand_pos;
     float* cv = a.cand_val + row * C;
     int32_t* ci = a.cand_idx + row * C;
-    for_each_element<T, CS, VEC>(zr, C, rank, [&](float x, int c) {
+    for_each_element<T, CS, VEC, NT>(zr, C, rank, [&](float x, int c) {
       if (sel_of(x)) {
         const int p = atomicAdd(pos_ctr, 1);
         cv[p] = x;
@@ -798,6 +814,18 @@ __global__ void __launch_bounds__(kST, stream_min_blocks<DEEP>())
     if (OUT == kOutCand && a.cand_count) a.cand_count[row] = kap;
     if (!yok) raise_status(a.status, 1);
   }
+}
+
+template <class T, int CS, bool VEC, int OUT, int SHAPE = kShapeWide>
+__global__ void __launch_bounds__(stream_threads<SHAPE>(), stream_min_blocks<SHAPE>())
+    fw_stream_rows_kernel(RowArgs a) {
+  allow_dependent_launch();
+  __shared__ StreamShared s;
+  stream_rows_body<T, CS, VEC, OUT, SHAPE>(a, s);
+  // A launch of the rows left over after the previous launch's whole waves
+  // starts early, as that launch's programmatic dependent; it ends only after
+  // that launch has completed, so the work queued after it sees every row.
+  if (a.wait_prior) wait_prior_grid();
 }
 
 }  // namespace fwb200

@@ -10,9 +10,12 @@
 //   2. n = |{z > t0}|; a unique maximum (n == 1) is solved on the spot
 //      (kappa = 1, h* = M - 1); otherwise the candidates are compacted into a
 //      per-group list by an exclusive shuffle scan;
-//   3. exact threshold: Michelot's fixed point on the list (michelot_list),
-//      or on the registers when the list would overflow (near-constant rows
-//      where most of the row is within 1 of the max);
+//   3. exact threshold: Michelot's fixed point with one candidate per lane
+//      when there are at most G of them (michelot_lane: counts are a
+//      ballot), on the list otherwise (michelot_list), or on the registers
+//      when the list would overflow (near-constant rows where most of the
+//      row is within 1 of the max); every form reduces the kept count first
+//      and the fp64 sum only while the kept set changes;
 //   4. output straight from the registers with the fp32 predicate z > H:
 //      the gradient grad_scale * ((1/kappa) [z > h*] - e_y), the support mask,
 //      or the support list.
@@ -31,8 +34,6 @@
 
 namespace fwb200 {
 
-constexpr int kWarpTierThreads = 256;
-constexpr int kWarpTierWarps = kWarpTierThreads / 32;
 constexpr int kWarpListCap = 128;  // list entries per warp, split between its groups
 
 // Column of register value (i, j) (slot i, element j) of lane `li` of a G-lane
@@ -164,27 +165,37 @@ __device__ __forceinline__ void warp_tier_nonfinite(const RowArgs& a, int64_t ro
   }
 }
 
-// Resident CTAs per SM the register budget is sized for: 4 (64 registers) up
-// to 32 values per lane, 1 at 64.  Short rows are latency-bound (a serial
-// chain per row: load, max, candidate scan, fp64 fixed point, write), so the
-// extra resident rows pay for the tighter register budget (B200: cfg3
-// 18.6 -> 17.2 us, cfg1 13.1 -> 12.0 us against 3 and 2 CTAs per SM).
+// Threads per CTA and resident CTAs per SM the register budget is sized
+// for, by register values per lane NV.  Short rows are latency- and
+// issue-bound (a serial chain per row: load, max, solve, write), so the
+// budgets keep every row of a few-thousand-row batch resident at once:
+//   NV <= 16   256 threads x 4 CTAs (64 registers);
+//   NV == 32   128 threads x 7 CTAs (73 registers, no spills): 4144 resident
+//              warps on 148 SMs, one per row of a 4096-row batch;
+//   NV == 64   256 threads x 1 CTA.
 template <int NV>
-constexpr int warp_tier_min_blocks() {
-  return NV <= 32 ? 4 : 1;
+__host__ __device__ constexpr int warp_tier_threads() {
+  return NV == 32 ? 128 : 256;
+}
+
+template <int NV>
+__host__ __device__ constexpr int warp_tier_min_blocks() {
+  return NV <= 16 ? 4 : (NV == 32 ? 7 : 1);
 }
 
 template <class T, int G, int NS, bool VEC, int OUT, bool FULLV>
-__global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS * Elem<T>::kEPS>())
+__global__ void __launch_bounds__(warp_tier_threads<NS * Elem<T>::kEPS>(),
+                                  warp_tier_min_blocks<NS * Elem<T>::kEPS>())
     fw_warp_rows_kernel(RowArgs a) {
   allow_dependent_launch();
   constexpr int EPS = Elem<T>::kEPS;
   constexpr int NV = NS * EPS;          // register values per lane
+  constexpr int WW = warp_tier_threads<NV>() / 32;  // warps per CTA
   constexpr int RPW = 32 / G;           // rows per warp
   constexpr int CAPG = kWarpListCap / RPW;
   static_assert(OUT == kOutGrad || OUT == kOutGradCols || OUT == kOutNone || sizeof(T) == 4,
                 "mask/candidate/shard outputs are fp32-only");
-  __shared__ float s_list[kWarpTierWarps][kWarpListCap];
+  __shared__ float s_list[WW][kWarpListCap];
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
   const int gi = lane / G;              // group in warp
@@ -192,10 +203,10 @@ __global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS * El
   const unsigned gmask = (G == 32) ? kFull : (((1u << G) - 1u) << (gi * G));
   float* L = &s_list[wib][gi * CAPG];
   const int C = (int)a.C;
-  const int64_t ngroups = (int64_t)gridDim.x * kWarpTierWarps * RPW;
+  const int64_t ngroups = (int64_t)gridDim.x * WW * RPW;
   const T* zbase = static_cast<const T*>(a.z);
 
-  for (int64_t row = ((int64_t)blockIdx.x * kWarpTierWarps + wib) * RPW + gi; row < a.B;
+  for (int64_t row = ((int64_t)blockIdx.x * WW + wib) * RPW + gi; row < a.B;
        row += ngroups) {
     const T* zr = zbase + row * a.ld;
     const int64_t ylab = a.y ? a.y[row] : -1;  // no labels in kOutShard
@@ -227,14 +238,15 @@ __global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS * El
       }
     }
 
+    // the label logit: its load is issued now, under the row's loads
+    const bool yok = (ylab >= 0 && ylab < a.C);
+    const int yc = yok ? (int)ylab : -1;
+    const float zy = yok ? ld_elem(zr + yc) : CUDART_NAN_F;
+
     float m = -CUDART_INF_F;
 #pragma unroll
     for (int s = 0; s < NV; ++s) m = max_nan(m, v[s]);
     m = group_max_nan<G>(m, gmask);
-
-    const bool yok = (ylab >= 0 && ylab < a.C);
-    const int yc = yok ? (int)ylab : -1;
-    const float zy = yok ? ld_elem(zr + yc) : CUDART_NAN_F;
 
     if (!isfinite(m)) {  // group-uniform; rare
       warp_tier_nonfinite<T, G, NS, VEC, OUT>(a, row, v, m, li, gmask, yc, zy);
@@ -260,36 +272,23 @@ __global__ void __launch_bounds__(kWarpTierThreads, warp_tier_min_blocks<NS * El
           if (v[s] > t0) L[off++] = v[s];
       }
       __syncwarp(gmask);
-      michelot_list<G, CAPG>(L, n, m, li, gmask, tau, kap);
+      if (n <= G)  // one candidate per lane
+        michelot_lane<G>(li < n ? L[li] : -CUDART_INF_F, n, m, gmask, tau, kap);
+      else
+        michelot_list<G, CAPG>(L, n, m, li, gmask, tau, kap);
       __syncwarp(gmask);
     } else {
-      // Same fixed point, evaluated on the registers (dense rows).
-      const double Md = (double)m;
-      double t = -CUDART_INF;
-      float Ht = t0;
-      int prev = -1;
-      for (int it = 0; it <= C; ++it) {
-        double sum = 0.0;
-        int cnt = 0;
-#pragma unroll
-        for (int s = 0; s < NV; ++s)
-          if (v[s] > Ht) { sum += (double)v[s] - Md; ++cnt; }
-        cnt = group_sum<G>(cnt, gmask);
-        sum = group_sum<G>(sum, gmask);
-        if (cnt == prev) break;
-        prev = cnt;
-        t = (sum - 1.0) / (double)cnt;
-        Ht = fmaxf(threshold_fp32(m, t), t0);
-      }
-      tau = t;
-      kap = prev;
+      // more candidates than the list holds (near-constant rows): the same
+      // fixed point on the registers
+      michelot_regs<G, NV>(v, m, t0, gmask, tau, kap);
     }
     const float Hf = threshold_fp32(m, tau);  // x > Hf <=> x in the support
 
     if (OUT == kOutGrad || OUT == kOutGradCols) {
       // Support entries first; the label entry is rewritten by lane 0 after a
       // group barrier (which orders the two stores to that address).
-      const float inv = (float)((double)a.scale / (double)kap);
+      // correctly rounded in fp32, equal to the fp64 quotient rounded to fp32
+      const float inv = __fdiv_rn(a.scale, (float)kap);
       T* gr = static_cast<T*>(a.grad) + row * a.ld;
 #pragma unroll
       for (int i = 0; i < NS; ++i) {

@@ -373,11 +373,22 @@ def test_half_precision_autograd(dtype):
     np.testing.assert_allclose(z.grad.float().cpu().numpy(), ref["grad"], rtol=rtol, atol=ATOL)
 
 
-# Batch sizes around the streaming tier's launch-shape switches on a 148-SM
-# B200: the cluster size (B * CS against 4 CTAs per SM), the deep-pipelining
-# instance (B * 8 <= 2 CTAs per SM) and the grid of one CTA per row.
-SHAPE_SWITCHES = [(1, 300000), (2, 65536), (37, 40000), (38, 40000), (73, 20000), (74, 20000),
-                  (147, 9000), (149, 9000), (295, 8200), (297, 8200), (600, 2049)]
+def _shape_switches():
+    """Batch sizes around the streaming tier's launch-plan switches for this
+    GPU's SM count (148 on a B200): deep shape with clusters of 8/4/2 or one
+    CTA per row (B <= 2 CTAs per SM), one wide launch (B <= 5 per SM, or a
+    last wave of more than 2 per SM), and a wide launch followed by a second,
+    deep launch of the rows left over after its whole waves (one CTA or a
+    cluster per leftover row)."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count if torch.cuda.is_available() else 148
+    deep, wide = 2 * sms, 5 * sms
+    return [(1, 300000), (2, 65536), (deep // 8, 40000), (deep // 8 + 1, 40000), (deep // 4 - 1, 20000),
+            (deep // 4, 20000), (deep // 2 - 1, 9000), (deep // 2 + 1, 9000), (deep - 1, 8200), (deep + 1, 8200),
+            (600, 2049), (wide + 20, 3000), (wide + 10, 70000), (wide + deep - 6, 9000),
+            (wide + deep + 4, 9000), (2 * wide + 7, 4100)]
+
+
+SHAPE_SWITCHES = _shape_switches()
 
 
 @pytest.mark.parametrize("B,C", SHAPE_SWITCHES, ids=[f"B{b}_C{c}" for b, c in SHAPE_SWITCHES])
@@ -403,3 +414,26 @@ def test_streaming_launch_shape_switches(B, C):
     expect = sel.astype(np.float64) / kap[:, None] / B
     expect[np.arange(B), y] -= 1.0 / B
     np.testing.assert_allclose(g, expect, rtol=RTOL, atol=ATOL)
+
+
+@pytest.mark.parametrize("B,C", SHAPE_SWITCHES[-5:], ids=[f"B{b}_C{c}" for b, c in SHAPE_SWITCHES[-5:]])
+def test_split_launch_followed_by_reduction(B, C):
+    """Where the rows left over after the wide launch's whole waves run as a
+    second, programmatically dependent launch, the loss reduction queued
+    right after (no host synchronisation in between) sees every row, and the
+    forward-only kernel gives the same kappa."""
+    from oracle import ref_cpu
+
+    rng = np.random.default_rng(7 * B + C)
+    z = rng.standard_normal((B, C)).astype(np.float32)
+    y = rng.integers(0, C, B).astype(np.int64)
+    _, kap, _, loss = ref_cpu.c_solve(z, y)
+    zt, yt = torch.from_numpy(z).cuda(), torch.from_numpy(y).cuda()
+    for _ in range(3):
+        _, _, l, k = capi.fused_fwd_bwd(zt, yt, 1.0 / B)
+        s = capi.loss_reduce(l, 1.0 / B)
+        _, _, kf = capi.forward_rows(zt, yt)
+        torch.cuda.synchronize()
+        np.testing.assert_allclose(s.item(), loss.mean(), rtol=1e-6)
+        np.testing.assert_array_equal(k.cpu().numpy(), kap)
+        np.testing.assert_array_equal(kf.cpu().numpy(), kap)
