@@ -68,11 +68,27 @@ cudaError_t dispatch_warp(const RowArgs& a, cudaStream_t st) {
 // waiting for that kernel before exiting (RowArgs::wait_prior).
 template <class T, int CS, bool VEC, int OUT, int SHAPE = kShapeWide>
 cudaError_t launch_stream_tier(const RowArgs& a, cudaStream_t st, bool after_prior = false) {
+  auto kernel = fw_stream_rows_kernel<T, CS, VEC, OUT, SHAPE>;
+  constexpr bool kStaged = (SHAPE == kShapeStaged && VEC);
+  if constexpr (kStaged) {
+    // the ring of stages is dynamic shared memory above the 48 KB default:
+    // raise the instance's limit once per device
+    static std::atomic<bool> attr_set[kMaxDevices] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return cudaErrorInvalidDevice;
+    if (dev >= kMaxDevices || !attr_set[dev].load(std::memory_order_acquire)) {
+      const cudaError_t e =
+          cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kStagedSmemBytes);
+      if (e != cudaSuccess) return e;
+      if (dev < kMaxDevices) attr_set[dev].store(true, std::memory_order_release);
+    }
+  }
   RowArgs b = a;
   b.wait_prior = after_prior ? 1 : 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(a.B * CS));
   cfg.blockDim = dim3(stream_threads<SHAPE>());
+  cfg.dynamicSmemBytes = kStaged ? kStagedSmemBytes : 0;
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   int n = 0;
@@ -90,7 +106,7 @@ cudaError_t launch_stream_tier(const RowArgs& a, cudaStream_t st, bool after_pri
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  return cudaLaunchKernelEx(&cfg, fw_stream_rows_kernel<T, CS, VEC, OUT, SHAPE>, b);
+  return cudaLaunchKernelEx(&cfg, kernel, b);
 }
 
 // The arguments for rows [r0, r0 + n) of a (every per-row pointer advanced).
@@ -122,20 +138,34 @@ inline int fit_cluster(int64_t rows, int64_t C, int64_t slots) {
   return cs;
 }
 
+// Few rows (at most two CTAs per SM): 16-byte-aligned rows take the staged
+// shape (bulk-copied tiles), the others the deep one.
 template <class T, bool VEC, int OUT>
 cudaError_t launch_deep(const RowArgs& a, cudaStream_t st, int cs, bool after_prior) {
+  constexpr int SH = VEC ? kShapeStaged : kShapeDeep;
   switch (cs) {
-    case 8: return launch_stream_tier<T, 8, VEC, OUT, kShapeDeep>(a, st, after_prior);
-    case 4: return launch_stream_tier<T, 4, VEC, OUT, kShapeDeep>(a, st, after_prior);
-    case 2: return launch_stream_tier<T, 2, VEC, OUT, kShapeDeep>(a, st, after_prior);
-    default: return launch_stream_tier<T, 1, VEC, OUT, kShapeDeep>(a, st, after_prior);
+    case 8: return launch_stream_tier<T, 8, VEC, OUT, SH>(a, st, after_prior);
+    case 4: return launch_stream_tier<T, 4, VEC, OUT, SH>(a, st, after_prior);
+    case 2: return launch_stream_tier<T, 2, VEC, OUT, SH>(a, st, after_prior);
+    default: return launch_stream_tier<T, 1, VEC, OUT, SH>(a, st, after_prior);
   }
 }
 
+// Long fp32 rows that write a gradient (or a gradient shard) stream through
+// the staged shape from this many columns on (B200, fraction of the HBM
+// roofline, wide / staged, fwd+bwd: C = 32000, 4096 rows 0.935 / 0.877;
+// C = 48000, 4096 rows 0.947 / 0.974; C = 65536, 1024 / 4096 rows 0.855 /
+// 0.890, 0.947 / 0.997; C = 128256, 8192 rows 0.959 / 1.005.  Forward only,
+// the wide shape stays ahead at every length: 0.984 / 0.711 at 65536 x 4096).
+constexpr int64_t kStagedMinCols = 40960;
+
 // Launch plan for B rows (one CTA per row; resident slots: 5 CTAs per SM of
-// the wide shape, 2 of the deep one):
-//  * B <= deep slots: the deep shape, with clusters of CS CTAs per row when
-//    rows x CS still fits one deep wave (e.g. 32 rows x 1e6 columns: CS 8);
+// the wide shape, 2 of the deep and staged ones):
+//  * B <= deep slots: the staged shape (the deep one for rows not 16-byte
+//    aligned), with clusters of CS CTAs per row when rows x CS still fits
+//    one such wave (e.g. 32 rows x 1e6 columns: CS 8);
+//  * long fp32 rows writing a gradient (C >= kStagedMinCols): one staged CTA
+//    per row;
 //  * otherwise one CTA per row in the wide shape; when that leaves a last
 //    wave of at most (deep slots) rows, those rows go to a second launch in
 //    the deep shape (clustered as above), started as a programmatic
@@ -148,6 +178,10 @@ cudaError_t dispatch_stream(const RowArgs& a, cudaStream_t st) {
   const int64_t deep = sms * stream_min_blocks<kShapeDeep>();
   const int64_t wide = sms * stream_min_blocks<kShapeWide>();
   if (a.B <= deep) return launch_deep<T, VEC, OUT>(a, st, fit_cluster(a.B, a.C, deep), false);
+  if constexpr (VEC && sizeof(T) == 4 && (OUT == kOutGrad || OUT == kOutShard)) {
+    // long fp32 rows that write a gradient: one staged CTA per row
+    if (a.C >= kStagedMinCols) return launch_stream_tier<T, 1, VEC, OUT, kShapeStaged>(a, st);
+  }
   const int64_t tail = a.B % wide;
   if (a.B <= wide || tail == 0 || tail > deep) return launch_stream_tier<T, 1, VEC, OUT>(a, st);
   const int64_t head = a.B - tail;

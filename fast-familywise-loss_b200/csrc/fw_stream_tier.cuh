@@ -56,20 +56,31 @@ constexpr int kSolveCap = 1024;       // gathered candidates per row
 constexpr int kStreamItems = 4;       // 16-byte loads per thread per streaming step (VEC)
 constexpr int kStreamScalars = 16;    // scalar loads per thread per streaming step (!VEC)
 
-// Launch shapes of the streaming kernel (16-byte loads in flight per thread,
-// resident CTAs per SM the register budget is sized for), 256 threads each:
-//   kShapeWide  4 loads, 5 CTAs per SM (<= 51 registers; 16-bit rows stream
-//               in half the time of fp32 ones, so more CTAs are needed to
-//               cover each row's exchange/solve/patch phase: B200, cfg2
-//               shape, bf16 99.1 -> 97.0 us, fp32 unchanged, six CTAs slower);
-//   kShapeDeep  8 loads, 2 CTAs per SM: grids of at most two CTAs per SM
-//               (very few rows, or the rows left over after whole waves),
-//               where few CTAs share an SM and each has to keep more bytes in
-//               flight (B200, B = 32 x C = 1e6 fp32 on clusters of 8:
-//               93.2 -> 83.1 us).
-// Without 16-byte loads (unaligned rows) both issue 16 scalar loads per
-// thread per step.
-enum StreamShape : int { kShapeWide = 0, kShapeDeep = 2 };
+// Launch shapes of the streaming kernel, 256 threads each (bytes in flight
+// per CTA, resident CTAs per SM the register budget is sized for):
+//   kShapeWide    four 16-byte register loads per thread (16 KB), 5 CTAs per
+//                 SM (<= 51 registers; 16-bit rows stream in half the time of
+//                 fp32 ones, so more CTAs are needed to cover each row's
+//                 exchange/solve/patch phase: B200, cfg2 shape, bf16 99.1 ->
+//                 97.0 us, fp32 unchanged, six CTAs slower);
+//   kShapeDeep    eight 16-byte register loads per thread (32 KB), 2 CTAs per
+//                 SM: grids of at most two CTAs per SM (very few rows, or the
+//                 rows left over after whole waves), where few CTAs share an
+//                 SM and each has to keep more bytes in flight (B200, B = 32 x
+//                 C = 1e6 fp32 on clusters of 8: 93.2 -> 83.1 us);
+//   kShapeStaged  16 KB tiles bulk-copied (cp.async.bulk, no multicast, this
+//                 GPU's own memory) into a ring of kStages shared-memory
+//                 stages (64 KB in flight, none of it in registers), 2 CTAs
+//                 per SM; 16-byte-aligned rows only (others stream as deep).
+// Without 16-byte loads (unaligned rows) every shape issues 16 scalar loads
+// per thread per step.
+enum StreamShape : int { kShapeWide = 0, kShapeDeep = 2, kShapeStaged = 3 };
+
+constexpr int kStages = 4;                                    // staged: tiles in flight per CTA
+constexpr int kStageItems = kST * kStreamItems;               // staged: 16-byte items per tile (16 KB)
+constexpr size_t kStagedSmemBytes = (size_t)kStages * kStageItems * 16;  // dynamic shared memory
+constexpr uint64_t kStageWaitLimitNs = 1000000000ull;         // 1 s; a tile lands in a few us
+constexpr uint64_t kStageDrainLimitNs = 100000000ull;         // 100 ms per stage after an abort
 
 template <int SHAPE>
 __host__ __device__ constexpr int stream_threads() {
@@ -78,7 +89,7 @@ __host__ __device__ constexpr int stream_threads() {
 
 template <bool VEC, int SHAPE = kShapeWide>
 __host__ __device__ constexpr int stream_ipt() {
-  return VEC ? (SHAPE == kShapeWide ? kStreamItems : 2 * kStreamItems) : kStreamScalars;
+  return VEC ? (SHAPE == kShapeDeep ? 2 * kStreamItems : kStreamItems) : kStreamScalars;
 }
 
 template <int SHAPE>
@@ -113,6 +124,9 @@ struct __align__(16) StreamShared {
   float row_max;
   int row_flags;    // bit-or of every CTA's flags
   int nsolve;
+  // staged shape: one mbarrier per stage, abort flag of a bounded wait
+  uint64_t stage_full[kStages];
+  int stage_abort;
   // dense-path decision, written by CTA 0 into every CTA of the cluster
   unsigned long long dec_cut;
   double dec_sum;
@@ -273,6 +287,12 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a, StreamShared&
     s.go_dense = 0;
     s.first_idx = INT_MAX;
     s.cand_pos = 0;
+    if constexpr (SHAPE == kShapeStaged) {
+      for (int k = 0; k < kStages; ++k) mbar_init(&s.stage_full[k], 1);
+      s.stage_abort = 0;
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
   }
   __syncthreads();
 
@@ -289,22 +309,9 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a, StreamShared&
   T* gr = (kZeroFill && a.grad) ? static_cast<T*>(a.grad) + row * a.ld : nullptr;
   uint8_t* mr = (OUT == kOutMask) ? a.mask + row * C : nullptr;
 
-  for (int64_t base = g.i0; base < g.i1; base += (int64_t)NT * IPT) {
-    float v[IPT * W];
-#pragma unroll
-    for (int u = 0; u < IPT; ++u) {
-      const int64_t it = base + (int64_t)u * NT + tid;
-      if (VEC) {
-        if (it < g.i1) {
-          unpack16<T>(ld_stream16(zr + W * it), &v[W * u]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < W; ++j) v[W * u + j] = -CUDART_INF_F;
-        }
-      } else {
-        v[u] = (it < g.i1) ? ld_elem(zr + it) : -CUDART_INF_F;
-      }
-    }
+  // One streaming step: this thread's IPT items base + u * NT + tid (values
+  // in v, -inf past the segment): zero output, running max, candidates.
+  auto consume = [&](float (&v)[IPT * W], int64_t base) {
 #pragma unroll
     for (int u = 0; u < IPT; ++u) {
       const int64_t it = base + (int64_t)u * NT + tid;
@@ -343,6 +350,82 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a, StreamShared&
           list_append(lz, li, wcnt, ovf, v[u * W + j], (int)(it * W + j),
                       v[u * W + j] > t, t, lane);
       }
+    }
+  };
+
+  if constexpr (SHAPE == kShapeStaged && VEC) {
+    // Tiles of kStageItems 16-byte items, bulk-copied into a ring of kStages
+    // shared-memory stages by thread 0 (one tile per stage in flight); all
+    // threads wait for a tile's mbarrier (bounded), consume it, and after a
+    // CTA barrier thread 0 refills the stage with the tile kStages ahead.
+    extern __shared__ __align__(16) uint4 stream_ring[];
+    const uint4* src = reinterpret_cast<const uint4*>(zr);
+    const int ntiles = (int)((g.i1 - g.i0 + kStageItems - 1) / kStageItems);
+    int issued = 0;  // thread 0: tiles issued so far
+    auto issue = [&](int k) {
+      const int st = k % kStages;
+      const int64_t first = g.i0 + (int64_t)k * kStageItems;
+      const int64_t n = (g.i1 - first < kStageItems) ? (g.i1 - first) : (int64_t)kStageItems;
+      const uint32_t bytes = (uint32_t)n * 16u;
+      mbar_expect_tx(&s.stage_full[st], bytes);
+      bulk_load(stream_ring + (size_t)st * kStageItems, src + first, bytes, &s.stage_full[st]);
+    };
+    if (tid == 0)
+      for (; issued < kStages && issued < ntiles; ++issued) issue(issued);
+    bool aborted = false;
+    for (int k = 0; k < ntiles; ++k) {
+      const int st = k % kStages;
+      const int64_t base = g.i0 + (int64_t)k * kStageItems;
+      bool ok = false;
+      if (!aborted) {
+        ok = mbar_wait_for(&s.stage_full[st], (uint32_t)(k / kStages) & 1u, kStageWaitLimitNs);
+        if (!ok) s.stage_abort = 1;
+      }
+      const uint4* tile = stream_ring + (size_t)st * kStageItems;
+      float v[IPT * W];
+#pragma unroll
+      for (int u = 0; u < IPT; ++u) {
+        const int l = u * NT + tid;
+        if (ok && base + l < g.i1) {
+          unpack16<T>(tile[l], &v[W * u]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < W; ++j) v[W * u + j] = -CUDART_INF_F;
+        }
+      }
+      consume(v, base);
+      __syncthreads();  // every thread is done with this stage
+      aborted = s.stage_abort != 0;
+      if (tid == 0 && !aborted && issued < ntiles) issue(issued++);
+    }
+    if (aborted && tid == 0) {
+      // a copy did not land in time: flag it, then let the copies already
+      // issued land (bounded) before this CTA's shared memory is released
+      raise_status(a.status, kStatusTimeout);
+      for (int st = 0; st < kStages; ++st) {
+        int last = -1;
+        for (int k = st; k < issued; k += kStages) last = k;
+        if (last >= 0) mbar_wait_for(&s.stage_full[st], (uint32_t)(last / kStages) & 1u, kStageDrainLimitNs);
+      }
+    }
+  } else {
+    for (int64_t base = g.i0; base < g.i1; base += (int64_t)NT * IPT) {
+      float v[IPT * W];
+#pragma unroll
+      for (int u = 0; u < IPT; ++u) {
+        const int64_t it = base + (int64_t)u * NT + tid;
+        if (VEC) {
+          if (it < g.i1) {
+            unpack16<T>(ld_stream16(zr + W * it), &v[W * u]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < W; ++j) v[W * u + j] = -CUDART_INF_F;
+          }
+        } else {
+          v[u] = (it < g.i1) ? ld_elem(zr + it) : -CUDART_INF_F;
+        }
+      }
+      consume(v, base);
     }
   }
   if (VEC && rank == CS - 1 && w == 0) {

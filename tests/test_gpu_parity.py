@@ -384,8 +384,8 @@ def _shape_switches():
     deep, wide = 2 * sms, 5 * sms
     return [(1, 300000), (2, 65536), (deep // 8, 40000), (deep // 8 + 1, 40000), (deep // 4 - 1, 20000),
             (deep // 4, 20000), (deep // 2 - 1, 9000), (deep // 2 + 1, 9000), (deep - 1, 8200), (deep + 1, 8200),
-            (600, 2049), (wide + 20, 3000), (wide + 10, 70000), (wide + deep - 6, 9000),
-            (wide + deep + 4, 9000), (2 * wide + 7, 4100)]
+            (deep + 10, 45000), (wide + 10, 70000), (600, 2049), (wide + 20, 3000), (wide + 10, 30000),
+            (wide + deep - 6, 9000), (wide + deep + 4, 9000), (2 * wide + 7, 4100)]
 
 
 SHAPE_SWITCHES = _shape_switches()
