@@ -120,6 +120,7 @@ struct __align__(16) StreamShared {
   float cta_max;
   int go_dense;     // written by CTA 0 after the gather
   int first_idx;
+  float label_z;    // the label's logit, stored by the thread that streams it
   int cand_pos;
   float row_max;
   int row_flags;    // bit-or of every CTA's flags
@@ -303,6 +304,14 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a, StreamShared&
   float run = -CUDART_INF_F;
   int wcnt = 0;
   bool ovf = false;
+  // The label and its item: the thread whose streaming step holds the label
+  // column records its value in its CTA's shared memory (a cluster's leader
+  // copies it from the owning CTA after the exchange barrier), so the solve
+  // needs no dependent global load.
+  const int64_t ylab = a.y ? a.y[row] : -1;  // no labels in kOutShard
+  const bool yok = (ylab >= 0 && ylab < C);
+  const int yc = yok ? (int)ylab : -1;
+  const int y_item = (yok && yc < (VEC ? EPS * (C / EPS) : C)) ? yc / W : -1;  // items < 2^31
   float* lz = s.lz[w];
   int* li = s.li[w];
   // kOutShard without a gradient shard (a.grad == null) only writes summaries
@@ -315,6 +324,12 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a, StreamShared&
 #pragma unroll
     for (int u = 0; u < IPT; ++u) {
       const int64_t it = base + (int64_t)u * NT + tid;
+      if ((int)it == y_item) {  // rare: this item holds the label column
+        const int jy = yc - y_item * W;
+#pragma unroll
+        for (int j = 0; j < W; ++j)
+          if (j == jy) s.label_z = v[u * W + j];
+      }
       if (it < g.i1) {
         if (kZeroFill && (OUT == kOutGrad || gr != nullptr)) {
           if (VEC)
@@ -441,6 +456,7 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a, StreamShared&
     const float shared_max = key_value(*reinterpret_cast<volatile unsigned*>(&s.run_key));
     const float t = __fsub_rd(fmaxf(run, shared_max), 1.0f);
     list_append(lz, li, wcnt, ovf, x, (int)c, x > t, t, lane);
+    if (in && c == yc) s.label_z = x;
   }
 
   // -------------------------------------------------------------- exchange
@@ -480,6 +496,16 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a, StreamShared&
       if (lane == 0) {
         s.row_max = rm;
         s.row_flags = flags;
+        if (leader && yok) {
+          // the label's logit from the CTA whose segment holds its column
+          // (the C % EPS tail columns belong to the last CTA)
+          int owner = CS - 1;
+          if (y_item >= 0) {
+            const int64_t n_items = VEC ? C / EPS : C;
+            while (owner > 0 && n_items * owner / CS > y_item) --owner;
+          }
+          s.label_z = cta_smem<CS>(&s, owner)->label_z;
+        }
       }
     }
     __syncthreads();
@@ -488,9 +514,6 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a, StreamShared&
   }
   const double Md = (double)M;
   const float t0 = __fsub_rd(M, 1.0f);
-  const int64_t ylab = a.y ? a.y[row] : -1;  // no labels in kOutShard
-  const bool yok = (ylab >= 0 && ylab < C);
-  const int yc = yok ? (int)ylab : -1;
 
   // ------------------------------------------------------- non-finite rows
   if (!isfinite(M)) {
@@ -510,7 +533,7 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a, StreamShared&
     row_barrier<CS>();
     if (!(leader && tid == 0)) return;
     const int j = s.nsolve;
-    const float zy = yok ? ld_elem(zr + yc) : CUDART_NAN_F;
+    const float zy = yok ? s.label_z : CUDART_NAN_F;
     if (OUT == kOutGrad) {
       st_elem(gr + j, a.scale - ((j == yc) ? a.scale : 0.0f));
       if (yok && j != yc) st_elem(gr + yc, -a.scale);
@@ -551,7 +574,40 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a, StreamShared&
     // finishes the row; the zero stores of the other warps precede the
     // barrier above, which orders them before warp 0's patch.
     static_assert(NW * kStreamListCap <= kSolveCap, "one CTA's lists must fit the solve list");
-    if (lists_ok && w != 0) return;
+    if (lists_ok) {
+      // every warp counts its own list's candidates above t0, takes its
+      // offset in the fixed order (warp, then list position) and copies
+      // them; then warp 0 alone solves and patches
+      int kept = 0;
+      for (int k0 = 0; k0 < wcnt; k0 += 32) {
+        const int k = k0 + lane;
+        kept += __popc(__ballot_sync(kFull, (k < wcnt) && (lz[k] > t0)));
+      }
+      if (lane == 0) s.gcnt[w] = kept;
+      __syncthreads();
+      int pos0 = 0, tot = 0;
+#pragma unroll
+      for (int ww = 0; ww < NW; ++ww) {
+        const int c = s.gcnt[ww];
+        pos0 += (ww < w) ? c : 0;
+        tot += c;
+      }
+      for (int k0 = 0; k0 < wcnt; k0 += 32) {
+        const int k = k0 + lane;
+        const float val = (k < wcnt) ? lz[k] : -CUDART_INF_F;
+        const bool keep = val > t0;
+        const unsigned b = __ballot_sync(kFull, keep);
+        if (keep) {
+          const int pos = pos0 + __popc(b & lanemask_lt(lane));
+          s.sz[pos] = val;
+          s.si[pos] = li[k];
+        }
+        pos0 += __popc(b);
+      }
+      if (w == 0 && lane == 0) s.nsolve = tot;
+      __syncthreads();
+      if (w != 0) return;
+    }
   }
   if constexpr (CS > 1) {
     // The leader CTA's warps gather the CS * NW lists in parallel (their
@@ -614,46 +670,8 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a, StreamShared&
         }
       }
     }
-  } else if (lists_ok && w == 0) {
-    int n = 0;
-    bool full = false;
-    for (int r = 0; r < CS && !full; ++r) {
-      const StreamShared* rs = cta_smem<CS>(&s, r);
-      for (int ww = 0; ww < NW && !full; ++ww) {
-        const int cnt = rs->wcnt[ww];
-        for (int k0 = 0; k0 < cnt; k0 += 32) {
-          const int k = k0 + lane;
-          float val = -CUDART_INF_F;
-          int col = 0;
-          if (k < cnt) {
-            val = rs->lz[ww][k];
-            col = rs->li[ww][k];
-          }
-          const bool keep = val > t0;
-          const unsigned b = __ballot_sync(kFull, keep);
-          if (n + __popc(b) > kSolveCap) {
-            full = true;
-            break;
-          }
-          if (keep) {
-            const int pos = n + __popc(b & lanemask_lt(lane));
-            s.sz[pos] = val;
-            s.si[pos] = col;
-          }
-          n += __popc(b);
-        }
-      }
-    }
-    if (lane == 0) {
-      s.nsolve = n;
-      for (int r = 0; r < CS; ++r) cta_smem<CS>(&s, r)->go_dense = full ? 1 : 0;
-    }
   }
-  if constexpr (CS == 1) {
-    __syncwarp();  // warp 0: the list and its size, written by the gather above
-  } else {
-    row_barrier<CS>();
-  }
+  if constexpr (CS > 1) row_barrier<CS>();
   const bool dense = (row_flags & 1) || s.go_dense;
 
   // ------------------------------------------------------ solve and patch
@@ -662,10 +680,13 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a, StreamShared&
     const int n = s.nsolve;
     double tau;
     int kap;
-    michelot_list<32>(s.sz, n, M, lane, kFull, tau, kap);
+    if (n <= 32)  // one candidate per lane
+      michelot_lane<32>(lane < n ? s.sz[lane] : -CUDART_INF_F, n, M, kFull, tau, kap);
+    else
+      michelot_list<32>(s.sz, n, M, lane, kFull, tau, kap);
     const float Hf = threshold_fp32(M, tau);  // x > Hf <=> x in the support
     if (OUT == kOutGrad) {
-      const float inv = (float)((double)a.scale / (double)kap);
+      const float inv = __fdiv_rn(a.scale, (float)kap);
       bool ysel = false;
       for (int k = lane; k < n; k += 32) {
         const int col = s.si[k];
@@ -738,7 +759,7 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a, StreamShared&
       if (lane == 0 && a.cand_count) a.cand_count[row] = kap;
     }
     if (lane == 0) {
-      const float zy = yok ? ld_elem(zr + yc) : CUDART_NAN_F;
+      const float zy = yok ? s.label_z : CUDART_NAN_F;
       if (a.H) a.H[row] = Hf;
       if (a.loss) a.loss[row] = yok ? row_loss(M, tau, zy) : CUDART_NAN_F;
       if (a.kappa) a.kappa[row] = kap;
@@ -890,7 +911,7 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a, StreamShared&
   }
   row_barrier<CS>();
   if (leader && tid == 0) {
-    const float zy = yok ? ld_elem(zr + yc) : CUDART_NAN_F;
+    const float zy = yok ? s.label_z : CUDART_NAN_F;
     if (a.H) a.H[row] = threshold_fp32(M, tau);
     if (a.loss) a.loss[row] = yok ? row_loss(M, tau, zy) : CUDART_NAN_F;
     if (a.kappa) a.kappa[row] = kap;
