@@ -69,7 +69,7 @@ cudaError_t dispatch_warp(const RowArgs& a, cudaStream_t st) {
 template <class T, int CS, bool VEC, int OUT, int SHAPE = kShapeWide>
 cudaError_t launch_stream_tier(const RowArgs& a, cudaStream_t st, bool after_prior = false) {
   auto kernel = fw_stream_rows_kernel<T, CS, VEC, OUT, SHAPE>;
-  constexpr bool kStaged = (SHAPE == kShapeStaged && VEC);
+  constexpr bool kStaged = (is_staged<SHAPE>() && VEC);
   if constexpr (kStaged) {
     // the ring of stages is dynamic shared memory above the 48 KB default:
     // raise the instance's limit once per device
@@ -78,7 +78,7 @@ cudaError_t launch_stream_tier(const RowArgs& a, cudaStream_t st, bool after_pri
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return cudaErrorInvalidDevice;
     if (dev >= kMaxDevices || !attr_set[dev].load(std::memory_order_acquire)) {
       const cudaError_t e =
-          cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kStagedSmemBytes);
+          cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)staged_smem_bytes<SHAPE>());
       if (e != cudaSuccess) return e;
       if (dev < kMaxDevices) attr_set[dev].store(true, std::memory_order_release);
     }
@@ -88,7 +88,7 @@ cudaError_t launch_stream_tier(const RowArgs& a, cudaStream_t st, bool after_pri
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(a.B * CS));
   cfg.blockDim = dim3(stream_threads<SHAPE>());
-  cfg.dynamicSmemBytes = kStaged ? kStagedSmemBytes : 0;
+  cfg.dynamicSmemBytes = kStaged ? staged_smem_bytes<SHAPE>() : 0;
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   int n = 0;
@@ -158,6 +158,12 @@ cudaError_t launch_deep(const RowArgs& a, cudaStream_t st, int cs, bool after_pr
 // 0.890, 0.947 / 0.997; C = 128256, 8192 rows 0.959 / 1.005.  Forward only,
 // the wide shape stays ahead at every length: 0.984 / 0.711 at 65536 x 4096).
 constexpr int64_t kStagedMinCols = 40960;
+// ... and through the 4-CTAs-per-SM staged shape (8 KB tiles) from this many
+// columns on, when the batch is more than one wave of the wide shape (B200,
+// C = 32000, wide / staged4: 1024 rows 0.788 / 0.827, 2048 rows 0.890 /
+// 0.916, 4096 rows 0.943 / 0.970; one wave or less the wide shape is ahead,
+// 512 rows 0.900 / 0.820; so are short rows, C = 8192 x 8192 0.854 / 0.762).
+constexpr int64_t kStaged4MinCols = 24576;
 
 // Launch plan for B rows (one CTA per row; resident slots: 5 CTAs per SM of
 // the wide shape, 2 of the deep and staged ones):
@@ -178,9 +184,20 @@ cudaError_t dispatch_stream(const RowArgs& a, cudaStream_t st) {
   const int64_t deep = sms * stream_min_blocks<kShapeDeep>();
   const int64_t wide = sms * stream_min_blocks<kShapeWide>();
   if (a.B <= deep) return launch_deep<T, VEC, OUT>(a, st, fit_cluster(a.B, a.C, deep), false);
-  if constexpr (VEC && sizeof(T) == 4 && (OUT == kOutGrad || OUT == kOutShard)) {
-    // long fp32 rows that write a gradient: one staged CTA per row
-    if (a.C >= kStagedMinCols) return launch_stream_tier<T, 1, VEC, OUT, kShapeStaged>(a, st);
+  if constexpr (VEC && (OUT == kOutGrad || OUT == kOutShard)) {
+    if constexpr (sizeof(T) == 4) {
+      // long fp32 rows that write a gradient: one staged CTA per row (2 per
+      // SM); mid-length ones over more than one wide wave: 4 per SM
+      if (a.C >= kStagedMinCols) return launch_stream_tier<T, 1, VEC, OUT, kShapeStaged>(a, st);
+      if (a.C >= kStaged4MinCols && a.B > wide) return launch_stream_tier<T, 1, VEC, OUT, kShapeStaged4>(a, st);
+    } else {
+      // 16-bit rows that write a gradient, over more than one wide wave:
+      // 4 staged CTAs per SM at any length from kStaged4MinCols on (B200,
+      // bf16, wide / staged4 / staged: 32000 x 4096 0.596 / 0.791 / 0.399;
+      // 128256 x 8192 0.897 / 1.003 / 0.731; 128256 x 1024 0.715 / 0.842 /
+      // 0.612)
+      if (a.C >= kStaged4MinCols && a.B > wide) return launch_stream_tier<T, 1, VEC, OUT, kShapeStaged4>(a, st);
+    }
   }
   const int64_t tail = a.B % wide;
   if (a.B <= wide || tail == 0 || tail > deep) return launch_stream_tier<T, 1, VEC, OUT>(a, st);

@@ -71,14 +71,13 @@ constexpr int kStreamScalars = 16;    // scalar loads per thread per streaming s
 //   kShapeStaged  16 KB tiles bulk-copied (cp.async.bulk, no multicast, this
 //                 GPU's own memory) into a ring of kStages shared-memory
 //                 stages (64 KB in flight, none of it in registers), 2 CTAs
-//                 per SM; 16-byte-aligned rows only (others stream as deep).
+//                 per SM; 16-byte-aligned rows only (others stream as deep);
+//   kShapeStaged4 the same with 8 KB tiles (32 KB in flight), 4 CTAs per SM.
 // Without 16-byte loads (unaligned rows) every shape issues 16 scalar loads
 // per thread per step.
-enum StreamShape : int { kShapeWide = 0, kShapeDeep = 2, kShapeStaged = 3 };
+enum StreamShape : int { kShapeWide = 0, kShapeDeep = 2, kShapeStaged = 3, kShapeStaged4 = 4 };
 
-constexpr int kStages = 4;                                    // staged: tiles in flight per CTA
-constexpr int kStageItems = kST * kStreamItems;               // staged: 16-byte items per tile (16 KB)
-constexpr size_t kStagedSmemBytes = (size_t)kStages * kStageItems * 16;  // dynamic shared memory
+constexpr int kStages = 4;                                    // staged shapes: tiles in flight per CTA
 constexpr uint64_t kStageWaitLimitNs = 1000000000ull;         // 1 s; a tile lands in a few us
 constexpr uint64_t kStageDrainLimitNs = 100000000ull;         // 100 ms per stage after an abort
 
@@ -89,12 +88,30 @@ __host__ __device__ constexpr int stream_threads() {
 
 template <bool VEC, int SHAPE = kShapeWide>
 __host__ __device__ constexpr int stream_ipt() {
-  return VEC ? (SHAPE == kShapeDeep ? 2 * kStreamItems : kStreamItems) : kStreamScalars;
+  return VEC ? (SHAPE == kShapeDeep ? 2 * kStreamItems : (SHAPE == kShapeStaged4 ? kStreamItems / 2 : kStreamItems))
+             : kStreamScalars;
 }
 
 template <int SHAPE>
 __host__ __device__ constexpr int stream_min_blocks() {
-  return SHAPE == kShapeWide ? 5 : 2;
+  return SHAPE == kShapeWide ? 5 : (SHAPE == kShapeStaged4 ? 4 : 2);
+}
+
+template <int SHAPE>
+__host__ __device__ constexpr bool is_staged() {
+  return SHAPE == kShapeStaged || SHAPE == kShapeStaged4;
+}
+
+// Staged shapes: 16-byte items per tile (one streaming step of every thread)
+// and the ring's dynamic shared memory.
+template <int SHAPE>
+__host__ __device__ constexpr int stage_items() {
+  return kST * stream_ipt<true, SHAPE>();
+}
+
+template <int SHAPE>
+__host__ __device__ constexpr size_t staged_smem_bytes() {
+  return (size_t)kStages * stage_items<SHAPE>() * 16;
 }
 
 // Waits until the grid launched before this one on the stream has completed
@@ -288,7 +305,7 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a, StreamShared&
     s.go_dense = 0;
     s.first_idx = INT_MAX;
     s.cand_pos = 0;
-    if constexpr (SHAPE == kShapeStaged) {
+    if constexpr (is_staged<SHAPE>()) {
       for (int k = 0; k < kStages; ++k) mbar_init(&s.stage_full[k], 1);
       s.stage_abort = 0;
       asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -353,22 +370,40 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a, StreamShared&
     if (lane == 0) atomicMax(&s.run_key, sort_key(run));
     const float shared_max = key_value(*reinterpret_cast<volatile unsigned*>(&s.run_key));
     const float t = __fsub_rd(fmaxf(run, shared_max), 1.0f);
-    bool anyc = false;
+    // candidates of this step: one count per lane, one warp scan for the
+    // offsets, then every lane stores its own in element order (the list
+    // holds them lane-major; a fixed order, so the solve stays deterministic)
+    int c = 0;
 #pragma unroll
-    for (int k = 0; k < IPT * W; ++k) anyc |= (v[k] > t);
-    if (__any_sync(kFull, anyc)) {
+    for (int k = 0; k < IPT * W; ++k) c += (v[k] > t) ? 1 : 0;
+    const int total = __reduce_add_sync(kFull, c);
+    if (total > 0 && !ovf) {
+      if (wcnt + total > kStreamListCap) {
+        wcnt = list_compact(lz, li, wcnt, t, lane);  // older entries at or below t
+        if (wcnt + total > kStreamListCap) ovf = true;
+      }
+      if (!ovf) {
+        int pos = wcnt + warp_excl_scan(c, lane);
+        if (c > 0) {
 #pragma unroll
-      for (int u = 0; u < IPT; ++u) {
-        const int64_t it = base + (int64_t)u * NT + tid;
+          for (int u = 0; u < IPT; ++u) {
+            const int col0 = (int)((base + (int64_t)u * NT + tid) * W);
 #pragma unroll
-        for (int j = 0; j < W; ++j)
-          list_append(lz, li, wcnt, ovf, v[u * W + j], (int)(it * W + j),
-                      v[u * W + j] > t, t, lane);
+            for (int j = 0; j < W; ++j)
+              if (v[u * W + j] > t) {
+                lz[pos] = v[u * W + j];
+                li[pos] = col0 + j;
+                ++pos;
+              }
+          }
+        }
+        wcnt += total;
       }
     }
   };
 
-  if constexpr (SHAPE == kShapeStaged && VEC) {
+  if constexpr (is_staged<SHAPE>() && VEC) {
+    constexpr int kStageItems = stage_items<SHAPE>();
     // Tiles of kStageItems 16-byte items, bulk-copied into a ring of kStages
     // shared-memory stages by thread 0 (one tile per stage in flight); all
     // threads wait for a tile's mbarrier (bounded), consume it, and after a

@@ -377,15 +377,16 @@ def _shape_switches():
     """Batch sizes around the streaming tier's launch-plan switches for this
     GPU's SM count (148 on a B200): deep shape with clusters of 8/4/2 or one
     CTA per row (B <= 2 CTAs per SM), one wide launch (B <= 5 per SM, or a
-    last wave of more than 2 per SM), and a wide launch followed by a second,
-    deep launch of the rows left over after its whole waves (one CTA or a
-    cluster per leftover row)."""
+    last wave of more than 2 per SM), staged tiles (2 or 4 CTAs per SM) for
+    long rows, and a wide launch followed by a second, staged launch of the
+    rows left over after its whole waves (one CTA or a cluster per leftover
+    row)."""
     sms = torch.cuda.get_device_properties(0).multi_processor_count if torch.cuda.is_available() else 148
     deep, wide = 2 * sms, 5 * sms
     return [(1, 300000), (2, 65536), (deep // 8, 40000), (deep // 8 + 1, 40000), (deep // 4 - 1, 20000),
             (deep // 4, 20000), (deep // 2 - 1, 9000), (deep // 2 + 1, 9000), (deep - 1, 8200), (deep + 1, 8200),
             (deep + 10, 45000), (wide + 10, 70000), (600, 2049), (wide + 20, 3000), (wide + 10, 30000),
-            (wide + deep - 6, 9000), (wide + deep + 4, 9000), (2 * wide + 7, 4100)]
+            (2 * wide + 3, 24600), (wide + deep - 6, 9000), (wide + deep + 4, 9000), (2 * wide + 7, 4100)]
 
 
 SHAPE_SWITCHES = _shape_switches()
@@ -437,3 +438,22 @@ def test_split_launch_followed_by_reduction(B, C):
         np.testing.assert_allclose(s.item(), loss.mean(), rtol=1e-6)
         np.testing.assert_array_equal(k.cpu().numpy(), kap)
         np.testing.assert_array_equal(kf.cpu().numpy(), kap)
+
+
+@pytest.mark.parametrize("B,C", [(6, 31623), (4, 300001), (9, 40002), (700, 30001)],
+                         ids=["cta_C31623", "cluster_C300001", "cluster_C40002", "wide_C30001"])
+def test_label_logit_captured_while_streaming(B, C):
+    """The streaming tier records the label's logit while it streams the row
+    (and a cluster's leader fetches it from the CTA whose segment holds it):
+    labels at column 0, in every CTA's segment, and in the C % 4 tail
+    columns give the oracle's per-row loss."""
+    rng = np.random.default_rng(B + C)
+    z = rng.standard_normal((B, C)).astype(np.float32)
+    y = np.linspace(0, C - 1, B).astype(np.int64)
+    y[0], y[-1] = 0, C - 1
+    if B > 2:
+        y[1] = C - 2
+    ref = O.solve(z, y, 1.0 / B)
+    out = _fused(z, y, 1.0 / B)
+    _check_row_outputs(out, z, y, ref, f"B{B}_C{C}")
+    np.testing.assert_allclose(out["grad"], ref["grad"], rtol=RTOL, atol=ATOL)
