@@ -11,9 +11,12 @@ deterministic loss reduction.  With N > 1 ranks (torchrun, one per GPU) the
 batch's B rows are split into contiguous row blocks (strong scaling, the
 metric's fixed B; --weak gives every rank B rows of its own), every rank runs
 the same step on its block with the gradient scaled by 1/B, and the global
-mean is combined by one scalar NCCL all-reduce per step, issued
-asynchronously so that it runs under the next step's kernel.  The K timed
-steps are captured once in a CUDA graph (kernels and NCCL call).
+mean is combined by one scalar NCCL all-reduce per step.  Each step's loss
+path (the loss reduction and the all-reduce) runs on a side stream after
+that step's kernel, under the next step's kernel: nothing of the next step
+reads the loss.  The K timed steps are captured once in a CUDA graph
+(kernels and NCCL calls), and every step's loss path is complete before the
+timed region closes.
 
 Printed JSON line (rank 0):
   value     rows/s of the whole job, inputs resident in HBM, device-timed with
@@ -424,25 +427,31 @@ def run_ours(a):
     scale = 1.0 / Bg
     stream = torch.cuda.current_stream(dev)
 
+    side = torch.cuda.Stream(dev)  # the scalar loss path of every step
+
     def steps(n, inputs=zs, rows_y=y, sc=scale, forward_only=False):
-        """n steps: the fused forward+backward (or the forward-only kernel),
-        the deterministic loss reduction, and with N > 1 ranks the scalar
-        all-reduce, issued asynchronously so that it runs under the next
-        step's kernel; the last one is waited for before returning."""
-        pend = None
+        """n steps: the fused forward+backward (or the forward-only kernel) on
+        the launching stream; each step's loss path -- the deterministic loss
+        reduction and, with N > 1 ranks, the scalar all-reduce -- on a side
+        stream after that step's kernel, so that it runs under the next
+        step's kernel (nothing of the next step reads the loss).  The side
+        stream is joined before returning: all n steps are complete."""
+        main = torch.cuda.current_stream(dev)
+        losses = []  # kept alive until the side stream has read them
         for i in range(n):
             zi = inputs[i % len(inputs)]
             if forward_only:
                 _, loss, _ = fw.forward_rows(zi, rows_y, None)
             else:
                 _, _, loss, _ = fw.fused_fwd_bwd(zi, rows_y, sc)
-            s = fw.loss_reduce(loss, sc)
-            if world > 1:
-                if pend is not None:
-                    pend.wait()
-                pend = dist.all_reduce(s, async_op=True)
-        if pend is not None:
-            pend.wait()
+            losses.append(loss)
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                s = fw.loss_reduce(loss, sc)
+                if world > 1:
+                    dist.all_reduce(s)
+        main.wait_stream(side)
+        del losses
 
     def kernels(n, inputs=zs, rows_y=y, forward_only=False):
         for i in range(n):
