@@ -70,9 +70,9 @@ RowArgs base_args(const void* z, const int64_t* y, int64_t B, int64_t C, int64_t
 
 // fp64 rows: a warp per row up to kF64WarpRowMaxC columns, a CTA per row
 // beyond; grid capped at the resident CTAs (rows are looped over).
-template <int TW, bool VEC>
+template <int TW, bool VEC, bool GRAD>
 cudaError_t launch_f64(const F64Args& a, cudaStream_t st) {
-  auto k = fw_f64_rows_kernel<TW, VEC>;
+  auto k = fw_f64_rows_kernel<TW, VEC, GRAD>;
   static std::atomic<int> occ_cache{0};
   int occ = occ_cache.load(std::memory_order_relaxed);
   if (occ == 0) {
@@ -91,10 +91,17 @@ cudaError_t launch_f64(const F64Args& a, cudaStream_t st) {
 int run_f64(const F64Args& a, cudaStream_t st) {
   const bool vec = aligned16(a.z) && (a.grad == nullptr || aligned16(a.grad)) && (a.ld % 2 == 0);
   cudaError_t e;
-  if (a.C <= kF64WarpRowMaxC)
-    e = vec ? launch_f64<1, true>(a, st) : launch_f64<1, false>(a, st);
-  else
-    e = vec ? launch_f64<kF64Warps, true>(a, st) : launch_f64<kF64Warps, false>(a, st);
+  if (a.grad) {
+    if (a.C <= kF64WarpRowMaxC)
+      e = vec ? launch_f64<1, true, true>(a, st) : launch_f64<1, false, true>(a, st);
+    else
+      e = vec ? launch_f64<kF64Warps, true, true>(a, st) : launch_f64<kF64Warps, false, true>(a, st);
+  } else {
+    if (a.C <= kF64WarpRowMaxC)
+      e = vec ? launch_f64<1, true, false>(a, st) : launch_f64<1, false, false>(a, st);
+    else
+      e = vec ? launch_f64<kF64Warps, true, false>(a, st) : launch_f64<kF64Warps, false, false>(a, st);
+  }
   return launch_status(e);
 }
 

@@ -52,7 +52,7 @@ struct F64Args {
   int64_t C;
   int64_t ld;
   double scale;      // gradient scale (1/B for "mean")
-  double* grad;      // [B, ld]; null: forward only (H, loss, kappa)
+  double* grad;      // [B, ld]; null: forward only (H, loss, kappa), the GRAD = false instance
   double* H;         // [B] or null
   double* loss;      // [B] or null
   int32_t* kappa;    // [B] or null
@@ -162,7 +162,8 @@ __device__ __forceinline__ void f64_team_sync() {
   }
 }
 
-template <int TW, bool VEC>
+// GRAD: write the gradient (a.grad); without it, forward only.
+template <int TW, bool VEC, bool GRAD>
 __global__ void __launch_bounds__(kF64Threads) fw_f64_rows_kernel(F64Args a) {
   allow_dependent_launch();
   constexpr int NT = 32 * TW;          // threads per row
@@ -196,7 +197,7 @@ __global__ void __launch_bounds__(kF64Threads) fw_f64_rows_kernel(F64Args a) {
     const int64_t row = row0 + team;
     if (row < a.B) {  // team-uniform (TW = 8: RPB = 1, block-uniform)
       const double* zr = a.z + row * a.ld;
-      double* gr = a.grad ? a.grad + row * a.ld : nullptr;
+      double* gr = GRAD ? a.grad + row * a.ld : nullptr;
       if (tt == 0) s_first[team] = INT_MAX;
 
       // ------------------------------------------------------------ stream
@@ -224,7 +225,7 @@ __global__ void __launch_bounds__(kF64Threads) fw_f64_rows_kernel(F64Args a) {
 #pragma unroll
         for (int u = 0; u < IPT; ++u) {
           const int64_t it = base + (int64_t)u * NT + tt;
-          if (gr && it < nitems) {
+          if (GRAD && it < nitems) {
             if (VEC)
               *reinterpret_cast<uint4*>(gr + 2 * it) = make_uint4(0u, 0u, 0u, 0u);
             else
@@ -252,7 +253,7 @@ __global__ void __launch_bounds__(kF64Threads) fw_f64_rows_kernel(F64Args a) {
       if (VEC && (C & 1) && tw == 0) {  // odd C: the last column
         const int64_t c = C - 1;
         const double x = (lane == 0) ? zr[c] : -CUDART_INF;
-        if (lane == 0 && gr) gr[c] = 0.0;
+        if (GRAD && lane == 0) gr[c] = 0.0;
         run = max_nan64(run, warp_max_nan64(x));
         const double t = __dsub_rd(run, 1.0);
         f64_list_append(lz, li, cnt, ovf, x, (int)c, x > t, t, lane);
@@ -304,8 +305,8 @@ __global__ void __launch_bounds__(kF64Threads) fw_f64_rows_kernel(F64Args a) {
         const int j = min(s_first[team], (int)(C - 1));
         if (tt == 0) {
           const double zy = yok ? zr[yc] : CUDART_NAN;
-          if (gr) gr[j] = a.scale - ((j == yc) ? a.scale : 0.0);
-          if (gr && yok && j != yc) gr[yc] = -a.scale;
+          if (GRAD) gr[j] = a.scale - ((j == yc) ? a.scale : 0.0);
+          if (GRAD && yok && j != yc) gr[yc] = -a.scale;
           if (a.H) a.H[row] = M;
           if (a.loss) a.loss[row] = yok ? (1.0 - zy + M) : CUDART_NAN;
           if (a.kappa) a.kappa[row] = 1;
@@ -371,12 +372,12 @@ __global__ void __launch_bounds__(kF64Threads) fw_f64_rows_kernel(F64Args a) {
                   gv -= a.scale;
                   ysel = true;
                 }
-                if (gr) gr[col] = gv;
+                if (GRAD) gr[col] = gv;
               }
             }
             ysel = __any_sync(kFull, ysel);
             if (lane == 0) {
-              if (gr && yok && !ysel) gr[yc] = -a.scale;
+              if (GRAD && yok && !ysel) gr[yc] = -a.scale;
               const double zy = yok ? zr[yc] : CUDART_NAN;
               if (a.H) a.H[row] = M + tau;
               if (a.loss) a.loss[row] = yok ? (1.0 + (M - zy)) + tau : CUDART_NAN;
@@ -425,14 +426,14 @@ __global__ void __launch_bounds__(kF64Threads) fw_f64_rows_kernel(F64Args a) {
           const double tau = t;
           const int kap = prev;
           const double inv = a.scale / (double)kap;
-          for (int64_t c = tt; gr && c < C; c += NT) {
+          for (int64_t c = tt; GRAD && c < C; c += NT) {
             const double x = zr[c];
             if (x > t0 && x - M > tau) gr[c] = inv;
           }
           f64_team_sync<TW>();
           if (tt == 0) {
             const double zy = yok ? zr[yc] : CUDART_NAN;
-            if (gr && yok) gr[yc] = ((zy > t0 && zy - M > tau) ? inv : 0.0) - a.scale;
+            if (GRAD && yok) gr[yc] = ((zy > t0 && zy - M > tau) ? inv : 0.0) - a.scale;
             if (a.H) a.H[row] = M + tau;
             if (a.loss) a.loss[row] = yok ? (1.0 + (M - zy)) + tau : CUDART_NAN;
             if (a.kappa) a.kappa[row] = kap;

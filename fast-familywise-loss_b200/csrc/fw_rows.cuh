@@ -66,22 +66,37 @@ cudaError_t dispatch_warp(const RowArgs& a, cudaStream_t st) {
 // after_prior: launched as a programmatic dependent of the previous kernel on
 // the stream (its CTAs may start while that kernel's last CTAs run) and
 // waiting for that kernel before exiting (RowArgs::wait_prior).
-template <class T, int CS, bool VEC, int OUT, int SHAPE = kShapeWide>
-cudaError_t launch_stream_tier(const RowArgs& a, cudaStream_t st, bool after_prior = false) {
-  auto kernel = fw_stream_rows_kernel<T, CS, VEC, OUT, SHAPE>;
-  constexpr bool kStaged = (is_staged<SHAPE>() && VEC);
-  if constexpr (kStaged) {
+template <class T, int CS, bool VEC, int OUT, int SHAPE>
+cudaError_t prepare_stream_instance() {
+  if constexpr (is_staged<SHAPE>() && VEC) {
     // the ring of stages is dynamic shared memory above the 48 KB default:
     // raise the instance's limit once per device
     static std::atomic<bool> attr_set[kMaxDevices] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return cudaErrorInvalidDevice;
     if (dev >= kMaxDevices || !attr_set[dev].load(std::memory_order_acquire)) {
-      const cudaError_t e =
-          cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)staged_smem_bytes<SHAPE>());
+      cudaError_t e = cudaFuncSetAttribute(fw_stream_rows_kernel<T, CS, VEC, OUT, SHAPE>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)staged_smem_bytes<SHAPE>());
+      // the whole unified L1 / shared array as shared memory: the narrow
+      // shape's 8 CTAs per SM need 227 KB of it (a preference, not a limit)
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(fw_stream_rows_kernel<T, CS, VEC, OUT, SHAPE>,
+                                 cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
       if (e != cudaSuccess) return e;
       if (dev < kMaxDevices) attr_set[dev].store(true, std::memory_order_release);
     }
+  }
+  return cudaSuccess;
+}
+
+template <class T, int CS, bool VEC, int OUT, int SHAPE = kShapeWide>
+cudaError_t launch_stream_tier(const RowArgs& a, cudaStream_t st, bool after_prior = false) {
+  auto kernel = fw_stream_rows_kernel<T, CS, VEC, OUT, SHAPE>;
+  constexpr bool kStaged = (is_staged<SHAPE>() && VEC);
+  {
+    const cudaError_t e = prepare_stream_instance<T, CS, VEC, OUT, SHAPE>();
+    if (e != cudaSuccess) return e;
   }
   RowArgs b = a;
   b.wait_prior = after_prior ? 1 : 0;
@@ -164,20 +179,40 @@ constexpr int64_t kStagedMinCols = 40960;
 // 0.916, 4096 rows 0.943 / 0.970; one wave or less the wide shape is ahead,
 // 512 rows 0.900 / 0.820; so are short rows, C = 8192 x 8192 0.854 / 0.762).
 constexpr int64_t kStaged4MinCols = 24576;
+// 16-bit rows writing a gradient take the staged4 shape from this many
+// columns on (B200, bf16, staged4 / narrow / wide: 65536 x 4096 0.959 /
+// 0.923 / 0.890; 128256 x 8192 1.003 / 0.979 / 0.931; 128256 x 1024 0.835 /
+// 0.748 / 0.713) ...
+constexpr int64_t kStaged4MinCols16 = 49152;
+// ... and shorter 16-bit rows, or fp32 rows of fewer than kNarrowMaxCols
+// columns, the narrow shape (1184 resident CTAs) once the batch holds this
+// many elements (B200, narrow / wide / staged4: bf16 32000 x 4096 0.876 /
+// 0.835 / 0.799, 32000 x 8192 0.950 / 0.883 / 0.839, 16000 x 8192 0.802 /
+// 0.756 / 0.649, 8192 x 16384 0.674 / 0.631 / 0.480; fp32 8192 x 8192 0.953 /
+// 0.908 / 0.765, 8192 x 16384 1.009 / 0.945 / 0.793; below it the wide shape
+// is ahead or level: bf16 32000 x 1024 0.698 / 0.703, 16000 x 2048 0.624 /
+// 0.674, fp32 8192 x 4096 0.858 / 0.853; longer fp32 rows stay with wide and
+// staged4: 16000 x 8192 0.966 / 0.969 / 0.980, 32000 x 4096 0.938 / 0.949 /
+// 0.976).
+constexpr int64_t kNarrowMinElems = int64_t(64) << 20;
+constexpr int64_t kNarrowMaxCols = 12288;
 
-// Launch plan for B rows (one CTA per row; resident slots: 5 CTAs per SM of
-// the wide shape, 2 of the deep and staged ones):
+// Launch plan for B rows (one CTA per row; resident slots per SM: wide 5,
+// deep and staged 2, staged4 4, narrow 8):
 //  * B <= deep slots: the staged shape (the deep one for rows not 16-byte
 //    aligned), with clusters of CS CTAs per row when rows x CS still fits
 //    one such wave (e.g. 32 rows x 1e6 columns: CS 8);
-//  * long fp32 rows writing a gradient (C >= kStagedMinCols): one staged CTA
-//    per row;
-//  * otherwise one CTA per row in the wide shape; when that leaves a last
-//    wave of at most (deep slots) rows, those rows go to a second launch in
-//    the deep shape (clustered as above), started as a programmatic
-//    dependent so that it runs under the first launch's last CTAs: a short
-//    last wave of the wide shape is latency-bound (B200, C = 32000 fp32:
-//    768 rows took 44.0 us against 22.6 us for 512 rows, 1024 rows 51.0 us).
+//  * 16-byte-aligned rows that write a gradient: the staged, staged4 or
+//    narrow shape by element size, row length and batch size (the
+//    constants above);
+//  * otherwise one CTA per row in the wide shape; when that is one full wave
+//    and a last wave of at most (deep slots) rows, those rows go to a second
+//    launch in the deep shape (clustered as above), started as a
+//    programmatic dependent so that it runs under the first launch's last
+//    CTAs: a short last wave of the wide shape is latency-bound (B200,
+//    C = 32000 fp32: 768 rows took 44.0 us against 22.6 us for 512 rows).
+//    Over more waves the CTAs have drifted apart and the second launch costs
+//    more than it saves (fp32 8192 x 8192: 95.9 us split, 90.3 us one launch).
 template <class T, bool VEC, int OUT>
 cudaError_t dispatch_stream(const RowArgs& a, cudaStream_t st) {
   const int64_t sms = sm_count();
@@ -185,22 +220,21 @@ cudaError_t dispatch_stream(const RowArgs& a, cudaStream_t st) {
   const int64_t wide = sms * stream_min_blocks<kShapeWide>();
   if (a.B <= deep) return launch_deep<T, VEC, OUT>(a, st, fit_cluster(a.B, a.C, deep), false);
   if constexpr (VEC && (OUT == kOutGrad || OUT == kOutShard)) {
+    const bool many = a.B * a.C >= kNarrowMinElems;
     if constexpr (sizeof(T) == 4) {
-      // long fp32 rows that write a gradient: one staged CTA per row (2 per
-      // SM); mid-length ones over more than one wide wave: 4 per SM
+      // long fp32 rows: one staged CTA per row (2 per SM); mid-length ones
+      // over more than one wide wave: 4 per SM; short ones in large batches:
+      // 8 narrow CTAs per SM
       if (a.C >= kStagedMinCols) return launch_stream_tier<T, 1, VEC, OUT, kShapeStaged>(a, st);
       if (a.C >= kStaged4MinCols && a.B > wide) return launch_stream_tier<T, 1, VEC, OUT, kShapeStaged4>(a, st);
+      if (a.C < kNarrowMaxCols && many) return launch_stream_tier<T, 1, VEC, OUT, kShapeNarrow>(a, st);
     } else {
-      // 16-bit rows that write a gradient, over more than one wide wave:
-      // 4 staged CTAs per SM at any length from kStaged4MinCols on (B200,
-      // bf16, wide / staged4 / staged: 32000 x 4096 0.596 / 0.791 / 0.399;
-      // 128256 x 8192 0.897 / 1.003 / 0.731; 128256 x 1024 0.715 / 0.842 /
-      // 0.612)
-      if (a.C >= kStaged4MinCols && a.B > wide) return launch_stream_tier<T, 1, VEC, OUT, kShapeStaged4>(a, st);
+      if (a.C >= kStaged4MinCols16 && a.B > wide) return launch_stream_tier<T, 1, VEC, OUT, kShapeStaged4>(a, st);
+      if (a.C < kStaged4MinCols16 && many) return launch_stream_tier<T, 1, VEC, OUT, kShapeNarrow>(a, st);
     }
   }
   const int64_t tail = a.B % wide;
-  if (a.B <= wide || tail == 0 || tail > deep) return launch_stream_tier<T, 1, VEC, OUT>(a, st);
+  if (a.B <= wide || a.B > 2 * wide || tail == 0 || tail > deep) return launch_stream_tier<T, 1, VEC, OUT>(a, st);
   const int64_t head = a.B - tail;
   const cudaError_t e = launch_stream_tier<T, 1, VEC, OUT>(rows_from<T>(a, 0, head), st);
   if (e != cudaSuccess) return e;

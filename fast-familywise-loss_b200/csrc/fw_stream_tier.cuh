@@ -49,10 +49,8 @@
 
 namespace fwb200 {
 
-constexpr int kST = 256;              // threads per CTA (wide and deep shapes; the most)
-constexpr int kSW = kST / 32;         // warps per CTA (the most: shared-memory sizing)
+constexpr int kST = 256;              // threads per CTA (all shapes but the narrow one)
 constexpr int kStreamListCap = 128;   // candidates per warp list
-constexpr int kSolveCap = 1024;       // gathered candidates per row
 constexpr int kStreamItems = 4;       // 16-byte loads per thread per streaming step (VEC)
 constexpr int kStreamScalars = 16;    // scalar loads per thread per streaming step (!VEC)
 
@@ -72,10 +70,13 @@ constexpr int kStreamScalars = 16;    // scalar loads per thread per streaming s
 //                 GPU's own memory) into a ring of kStages shared-memory
 //                 stages (64 KB in flight, none of it in registers), 2 CTAs
 //                 per SM; 16-byte-aligned rows only (others stream as deep);
-//   kShapeStaged4 the same with 8 KB tiles (32 KB in flight), 4 CTAs per SM.
+//   kShapeStaged4 the same with 8 KB tiles (32 KB in flight), 4 CTAs per SM;
+//   kShapeNarrow  128 threads, 4 KB tiles (16 KB in flight), 8 CTAs per SM:
+//                 1184 resident CTAs, so that batches of up to that many rows
+//                 run as one wave (one ramp and one solve phase per launch).
 // Without 16-byte loads (unaligned rows) every shape issues 16 scalar loads
 // per thread per step.
-enum StreamShape : int { kShapeWide = 0, kShapeDeep = 2, kShapeStaged = 3, kShapeStaged4 = 4 };
+enum StreamShape : int { kShapeWide = 0, kShapeDeep = 2, kShapeStaged = 3, kShapeStaged4 = 4, kShapeNarrow = 5 };
 
 constexpr int kStages = 4;                                    // staged shapes: tiles in flight per CTA
 constexpr uint64_t kStageWaitLimitNs = 1000000000ull;         // 1 s; a tile lands in a few us
@@ -83,30 +84,32 @@ constexpr uint64_t kStageDrainLimitNs = 100000000ull;         // 100 ms per stag
 
 template <int SHAPE>
 __host__ __device__ constexpr int stream_threads() {
-  return kST;
+  return SHAPE == kShapeNarrow ? 128 : kST;
 }
 
 template <bool VEC, int SHAPE = kShapeWide>
 __host__ __device__ constexpr int stream_ipt() {
-  return VEC ? (SHAPE == kShapeDeep ? 2 * kStreamItems : (SHAPE == kShapeStaged4 ? kStreamItems / 2 : kStreamItems))
+  return VEC ? (SHAPE == kShapeDeep ? 2 * kStreamItems
+                                    : ((SHAPE == kShapeStaged4 || SHAPE == kShapeNarrow) ? kStreamItems / 2
+                                                                                         : kStreamItems))
              : kStreamScalars;
 }
 
 template <int SHAPE>
 __host__ __device__ constexpr int stream_min_blocks() {
-  return SHAPE == kShapeWide ? 5 : (SHAPE == kShapeStaged4 ? 4 : 2);
+  return SHAPE == kShapeWide ? 5 : (SHAPE == kShapeStaged4 ? 4 : (SHAPE == kShapeNarrow ? 8 : 2));
 }
 
 template <int SHAPE>
 __host__ __device__ constexpr bool is_staged() {
-  return SHAPE == kShapeStaged || SHAPE == kShapeStaged4;
+  return SHAPE == kShapeStaged || SHAPE == kShapeStaged4 || SHAPE == kShapeNarrow;
 }
 
 // Staged shapes: 16-byte items per tile (one streaming step of every thread)
 // and the ring's dynamic shared memory.
 template <int SHAPE>
 __host__ __device__ constexpr int stage_items() {
-  return kST * stream_ipt<true, SHAPE>();
+  return stream_threads<SHAPE>() * stream_ipt<true, SHAPE>();
 }
 
 template <int SHAPE>
@@ -121,17 +124,20 @@ __device__ __forceinline__ void wait_prior_grid() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
+// Shared state of one CTA with NW warps.
+template <int NW>
 struct __align__(16) StreamShared {
-  float lz[kSW][kStreamListCap];
-  int li[kSW][kStreamListCap];
-  float sz[kSolveCap];
-  int si[kSolveCap];
+  static constexpr int kSolve = NW * kStreamListCap;  // gathered candidates per row
+  float lz[NW][kStreamListCap];
+  int li[NW][kStreamListCap];
+  float sz[kSolve];
+  int si[kSolve];
   double hs[256];
   int hc[256];
-  float wmax[kSW];
-  int wcnt[kSW];
-  int gcnt[8 * kSW];  // cluster gather: kept candidates per (rank, warp) list
-  int goff[8 * kSW];  // and their offsets in the solve list
+  float wmax[NW];
+  int wcnt[NW];
+  int gcnt[8 * NW];  // cluster gather: kept candidates per (rank, warp) list
+  int goff[8 * NW];  // and their offsets in the solve list
   unsigned run_key;
   int flags;        // bit 0: a warp list overflowed
   float cta_max;
@@ -152,8 +158,8 @@ struct __align__(16) StreamShared {
   int dec_cnt, dec_done;
 };
 
-template <int CS>
-__device__ __forceinline__ StreamShared* cta_smem(StreamShared* s, int rank) {
+template <int CS, class S>
+__device__ __forceinline__ S* cta_smem(S* s, int rank) {
   if constexpr (CS > 1) {
     return cooperative_groups::this_cluster().map_shared_rank(s, rank);
   } else {
@@ -282,9 +288,11 @@ __device__ __forceinline__ void for_each_element(const T* zr, int64_t C,
 }
 
 template <class T, int CS, bool VEC, int OUT, int SHAPE>
-__device__ __forceinline__ void stream_rows_body(const RowArgs& a, StreamShared& s) {
+__device__ __forceinline__ void stream_rows_body(const RowArgs& a,
+                                                 StreamShared<stream_threads<SHAPE>() / 32>& s) {
   constexpr int NT = stream_threads<SHAPE>();  // threads per CTA
   constexpr int NW = NT / 32;                  // warps per CTA
+  using SS = StreamShared<NW>;
   static_assert(OUT == kOutGrad || OUT == kOutNone || sizeof(T) == 4,
                 "mask/candidate/shard outputs are fp32-only");
   constexpr bool kZeroFill = (OUT == kOutGrad || OUT == kOutShard);
@@ -522,7 +530,7 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a, StreamShared&
       float rm = -CUDART_INF_F;
       int flags = 0;
       if (lane < CS) {
-        const StreamShared* rs = cta_smem<CS>(&s, lane);
+        const SS* rs = cta_smem<CS>(&s, lane);
         rm = rs->cta_max;
         flags = rs->flags;
       }
@@ -604,11 +612,11 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a, StreamShared&
   // ---------------------------------------------------------------- gather
   const bool lists_ok = !(row_flags & 1);  // no warp list overflowed
   if constexpr (CS == 1) {
-    // One CTA: the warp lists hold at most NW * kStreamListCap <= kSolveCap
+    // One CTA: the warp lists hold at most NW * kStreamListCap = SS::kSolve
     // candidates, so the gathered list cannot overflow and warp 0 alone
     // finishes the row; the zero stores of the other warps precede the
     // barrier above, which orders them before warp 0's patch.
-    static_assert(NW * kStreamListCap <= kSolveCap, "one CTA's lists must fit the solve list");
+    static_assert(NW * kStreamListCap <= SS::kSolve, "one CTA's lists must fit the solve list");
     if (lists_ok) {
       // every warp counts its own list's candidates above t0, takes its
       // offset in the fixed order (warp, then list position) and copies
@@ -652,7 +660,7 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a, StreamShared&
     if (lists_ok && leader) {
       constexpr int NL = CS * NW;
       for (int L = w; L < NL; L += NW) {
-        const StreamShared* rs = cta_smem<CS>(&s, L / NW);
+        const SS* rs = cta_smem<CS>(&s, L / NW);
         const int ww = L % NW;
         const int cnt = rs->wcnt[ww];
         int kept = 0;
@@ -673,7 +681,7 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a, StreamShared&
           tot += __reduce_add_sync(kFull, c);
         }
         if (lane == 0) {
-          const bool full = tot > kSolveCap;
+          const bool full = tot > SS::kSolve;
           s.nsolve = full ? 0 : tot;
           for (int r = 0; r < CS; ++r) cta_smem<CS>(&s, r)->go_dense = full ? 1 : 0;
         }
@@ -681,7 +689,7 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a, StreamShared&
       __syncthreads();
       if (!s.go_dense) {
         for (int L = w; L < NL; L += NW) {
-          const StreamShared* rs = cta_smem<CS>(&s, L / NW);
+          const SS* rs = cta_smem<CS>(&s, L / NW);
           const int ww = L % NW;
           const int cnt = rs->wcnt[ww];
           int pos0 = s.goff[L];
@@ -832,7 +840,7 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a, StreamShared&
           int c = s.hc[b];
           double sm = s.hs[b];
           for (int r = 1; r < CS; ++r) {
-            const StreamShared* rs = cta_smem<CS>(&s, r);
+            const SS* rs = cta_smem<CS>(&s, r);
             c += rs->hc[b];
             sm += rs->hs[b];
           }
@@ -874,7 +882,7 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a, StreamShared&
         }
         if (!refine) done = true;
         for (int r = 0; r < CS; ++r) {
-          StreamShared* rs = cta_smem<CS>(&s, r);
+          SS* rs = cta_smem<CS>(&s, r);
           rs->dec_prefix = prefix;
           rs->dec_mask = pmask;
           rs->dec_cnt = cnt_a;
@@ -959,7 +967,7 @@ template <class T, int CS, bool VEC, int OUT, int SHAPE = kShapeWide>
 __global__ void __launch_bounds__(stream_threads<SHAPE>(), stream_min_blocks<SHAPE>())
     fw_stream_rows_kernel(RowArgs a) {
   allow_dependent_launch();
-  __shared__ StreamShared s;
+  __shared__ StreamShared<stream_threads<SHAPE>() / 32> s;
   stream_rows_body<T, CS, VEC, OUT, SHAPE>(a, s);
   // A launch of the rows left over after the previous launch's whole waves
   // starts early, as that launch's programmatic dependent; it ends only after

@@ -323,6 +323,54 @@ def test_half_precision_logits(dtype, name):
     np.testing.assert_allclose(grad.float().cpu().numpy(), 2.0 * ref["grad"], rtol=2 * rtol, atol=ATOL)
 
 
+def _half_shape_switches():
+    """16-bit batches on both sides of the streaming tier's 16-bit launch-plan
+    switches (148 SMs on a B200): the narrow shape (short rows, >= 64 Mi
+    elements), the staged4 shape (>= 49152 columns over more than one wide
+    wave), one wide launch, and a wide launch followed by a second launch of
+    the rows left over after its whole wave."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count if torch.cuda.is_available() else 148
+    deep, wide = 2 * sms, 5 * sms
+    n64 = 64 << 20
+    return [(n64 // 32000 + 1, 32000), (n64 // 32000 - 1, 32000), (wide + 1, 49152), (wide + 1, 49151),
+            (wide + 20, 30000), (n64 // 8192 + 3, 8192)]
+
+
+HALF_SWITCHES = _half_shape_switches()
+
+
+@pytest.mark.parametrize("dtype", list(HALF_TYPES))
+@pytest.mark.parametrize("B,C", HALF_SWITCHES, ids=[f"B{b}_C{c}" for b, c in HALF_SWITCHES])
+def test_half_precision_launch_shapes(dtype, B, C):
+    """16-bit logits through every launch shape the plan picks for them:
+    kappa bit-exact and H, loss within tolerance against the C oracle on the
+    rounded values, the gradient within the element type's unit roundoff;
+    odd rows are near-ties (sigma 1e-2 in 16-bit: many candidates)."""
+    from oracle import ref_cpu
+
+    tdt, rtol = HALF_TYPES[dtype]
+    rng = np.random.default_rng(B + 7 * C)
+    z32 = rng.standard_normal((B, C)).astype(np.float32)
+    z32[1::2] *= np.float32(1e-2)
+    zh = torch.from_numpy(z32).to(tdt)
+    z = zh.float().numpy()
+    del z32
+    y = rng.integers(0, C, B).astype(np.int64)
+    tau, kap, M, loss = ref_cpu.c_solve(z, y)
+    grad, H, lo, kappa = capi.fused_fwd_bwd(zh.cuda(), torch.from_numpy(y).cuda(), 1.0 / B)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(kappa.cpu().numpy(), kap)
+    Hr = O.threshold_f32(tau, M)
+    np.testing.assert_allclose(H.cpu().numpy(), Hr, rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(lo.cpu().numpy(), loss, rtol=RTOL, atol=ATOL)
+    g = grad.float().cpu().numpy()
+    del grad
+    expect = (z > Hr[:, None]).astype(np.float32) / kap[:, None].astype(np.float32) / np.float32(B)
+    expect[np.arange(B), y] -= np.float32(1.0 / B)
+    np.testing.assert_allclose(g, expect, rtol=rtol, atol=ATOL)
+    torch.cuda.empty_cache()
+
+
 @pytest.mark.parametrize("dtype", list(HALF_TYPES))
 @pytest.mark.parametrize("C", [100, 5000])
 def test_half_precision_subnormal_candidates(dtype, C):
@@ -378,15 +426,17 @@ def _shape_switches():
     GPU's SM count (148 on a B200): deep shape with clusters of 8/4/2 or one
     CTA per row (B <= 2 CTAs per SM), one wide launch (B <= 5 per SM, or a
     last wave of more than 2 per SM), staged tiles (2 or 4 CTAs per SM) for
-    long rows, and a wide launch followed by a second, staged launch of the
-    rows left over after its whole waves (one CTA or a cluster per leftover
-    row)."""
+    long rows, the narrow staged shape (8 CTAs per SM) for short rows in
+    batches of >= 64 Mi elements, and a wide launch followed by a second,
+    staged launch of the rows left over after its one whole wave (one CTA or
+    a cluster per leftover row)."""
     sms = torch.cuda.get_device_properties(0).multi_processor_count if torch.cuda.is_available() else 148
     deep, wide = 2 * sms, 5 * sms
     return [(1, 300000), (2, 65536), (deep // 8, 40000), (deep // 8 + 1, 40000), (deep // 4 - 1, 20000),
             (deep // 4, 20000), (deep // 2 - 1, 9000), (deep // 2 + 1, 9000), (deep - 1, 8200), (deep + 1, 8200),
             (deep + 10, 45000), (wide + 10, 70000), (600, 2049), (wide + 20, 3000), (wide + 10, 30000),
-            (2 * wide + 3, 24600), (wide + deep - 6, 9000), (wide + deep + 4, 9000), (2 * wide + 7, 4100)]
+            (2 * wide + 3, 24600), ((64 << 20) // 12287 + 1, 12287), ((64 << 20) // 12287, 12287),
+            (wide + deep - 6, 9000), (wide + deep + 4, 9000), (2 * wide + 7, 4100)]
 
 
 SHAPE_SWITCHES = _shape_switches()

@@ -1,7 +1,7 @@
 """Row-sharded FW loss through the public API
 (fwloss_b200.distributed.sharded_familywise_loss) over NCCL, one process per
-GPU: in a one-rank group on any GPU box and across two GPUs where the box has
-them.  The checks themselves are in tests/rows_sharded_worker.py (loss and
+GPU: in a one-rank group on any GPU box and across two and four GPUs where the
+box has them.  The checks themselves are in tests/rows_sharded_worker.py (loss and
 gradient rows against familywise_loss on the whole batch, the forward-only
 path, and the step captured in a CUDA graph with its NCCL all-reduce)."""
 import os
@@ -25,7 +25,7 @@ def _free_port():
     return port
 
 
-@pytest.mark.parametrize("nproc", [1, 2])
+@pytest.mark.parametrize("nproc", [1, 2, 4])
 def test_rows_sharded_nccl(nproc):
     if torch.cuda.device_count() < nproc:
         pytest.skip(f"needs {nproc} GPUs")
