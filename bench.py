@@ -11,12 +11,13 @@ deterministic loss reduction.  With N > 1 ranks (torchrun, one per GPU) the
 batch's B rows are split into contiguous row blocks (strong scaling, the
 metric's fixed B; --weak gives every rank B rows of its own), every rank runs
 the same step on its block with the gradient scaled by 1/B, and the global
-mean is combined by one scalar NCCL all-reduce per step.  Each step's loss
-path (the loss reduction and the all-reduce) runs on a side stream after
+mean is combined per step by the cross-GPU loss sum: one kernel that reduces
+the rank's losses and exchanges the partials over NVLink peer memory
+(fw_loss_allreduce; the loss reduction + a scalar NCCL all-reduce where the
+GPUs lack peer access).  Each step's loss path runs on a side stream after
 that step's kernel, under the next step's kernel: nothing of the next step
-reads the loss.  The K timed steps are captured once in a CUDA graph
-(kernels and NCCL calls), and every step's loss path is complete before the
-timed region closes.
+reads the loss.  The K timed steps are captured once in a CUDA graph, and
+every step's loss path is complete before the timed region closes.
 
 Printed JSON line (rank 0):
   value     rows/s of the whole job, inputs resident in HBM, device-timed with
@@ -109,7 +110,7 @@ def bench_config(name, world, strong=True, esize=4):
                     f"{dict([(8, 'fp64'), (4, 'fp32'), (2, '16-bit')])[esize]} logits "
                     f"{kinds.get(name, 'N(0,1)' if name.startswith('gauss') else '')}, int64 labels",
         "rows_per_gpu": rows, "classes": C, "global_batch": Bg,
-        "parallelism": f"row-sharded dp{world}" + (" + scalar NCCL all-reduce" if world > 1 else ""),
+        "parallelism": f"row-sharded dp{world}" + (" + cross-GPU scalar loss sum" if world > 1 else ""),
         "l2": f"inputs {per / 1e6:.1f} MB logits + {per / 1e6:.1f} MB gradient per step and GPU"
               + (" (> 3x the 126 MB L2, no flush needed)" if per > 3 * L2_BYTES else
                  f" (rotating over {min(64, -(-3 * L2_BYTES // per))} input copies)"),
@@ -428,11 +429,15 @@ def run_ours(a):
     stream = torch.cuda.current_stream(dev)
 
     side = torch.cuda.Stream(dev)  # the scalar loss path of every step
+    # N > 1: the cross-GPU loss sum as one kernel over peer memory (built
+    # collectively here, before any capture); None without peer access
+    from fwloss_b200.distributed import loss_exchange
+    exchange = loss_exchange(None, dev) if world > 1 else None
 
     def steps(n, inputs=zs, rows_y=y, sc=scale, forward_only=False):
         """n steps: the fused forward+backward (or the forward-only kernel) on
         the launching stream; each step's loss path -- the deterministic loss
-        reduction and, with N > 1 ranks, the scalar all-reduce -- on a side
+        reduction, with N > 1 ranks fused with the cross-GPU sum -- on a side
         stream after that step's kernel, so that it runs under the next
         step's kernel (nothing of the next step reads the loss).  The side
         stream is joined before returning: all n steps are complete."""
@@ -447,9 +452,12 @@ def run_ours(a):
             losses.append(loss)
             side.wait_stream(main)
             with torch.cuda.stream(side):
-                s = fw.loss_reduce(loss, sc)
-                if world > 1:
-                    dist.all_reduce(s)
+                if exchange is not None:
+                    exchange.reduce(loss, sc)
+                else:
+                    s = fw.loss_reduce(loss, sc)
+                    if world > 1:
+                        dist.all_reduce(s)
         main.wait_stream(side)
         del losses
 
@@ -609,7 +617,7 @@ def run_ours(a):
                    "sample": f"failed: {ex!r}"[:200]}
 
     if rank == 0:
-        launches_per_step = 2  # fused kernel + loss reduction (the NCCL all-reduce is NCCL's)
+        launches_per_step = 2  # fused kernel + loss reduction (with N > 1: + the cross-GPU sum, same kernel)
         traffic = rows_traffic(profile_traffic(a.config if a.dtype == "f32" else f"{a.config}_{a.dtype}"), B,
                                B_cfg)
         line = {
@@ -633,6 +641,9 @@ def run_ours(a):
         }
         if weak is not None:
             line["weak"] = weak
+        if world > 1:
+            line["loss_sum"] = ("fw_loss_allreduce (loss reduction + NVLink peer-memory exchange, one kernel)"
+                                if exchange is not None else "fw_loss_reduce + NCCL all-reduce")
         print(json.dumps(line), flush=True)
     run_steps = g_steps = None  # graphs holding NCCL calls go before the process group
     torch.cuda.synchronize(dev)

@@ -6,6 +6,7 @@
 #include <cooperative_groups.h>
 
 #include "fw_device.cuh"
+#include "fw_reduce.cuh"
 
 namespace fwb200 {
 
@@ -201,31 +202,6 @@ __global__ void __launch_bounds__(kAuxThreads)
 // on the stream (usually the one that wrote the losses): it may be scheduled
 // while that kernel drains, and griddepcontrol.wait holds every thread until
 // that kernel has completed and its writes are visible.  T: fp32 or fp64.
-constexpr int kReduceCluster = 8;
-constexpr int64_t kReduceClusterMinRows = 16384;  // B above which CL = kReduceCluster
-constexpr int kReduceThreads = 512;
-constexpr int kReduceBatch = 4;  // 16-byte loads in flight per thread
-
-// Sixteen bytes of T (four floats or two doubles) per load.
-template <class T>
-struct Vec16;
-template <>
-struct Vec16<float> {
-  static constexpr int N = 4;
-  __device__ static void load(const float* p, double (&v)[4]) {
-    const float4 x = *reinterpret_cast<const float4*>(p);
-    v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
-  }
-};
-template <>
-struct Vec16<double> {
-  static constexpr int N = 2;
-  __device__ static void load(const double* p, double (&v)[2]) {
-    const double2 x = *reinterpret_cast<const double2*>(p);
-    v[0] = x.x; v[1] = x.y;
-  }
-};
-
 template <class T, int CL>
 __global__ void __launch_bounds__(kReduceThreads)
     fw_loss_reduce_kernel(const T* __restrict__ loss, int64_t B,
@@ -238,25 +214,7 @@ __global__ void __launch_bounds__(kReduceThreads)
   const int64_t ngroups = (B + N - 1) / N;
   const int64_t g_lo = ngroups * rank / CL;
   const int64_t g_hi = ngroups * (rank + 1) / CL;
-  double s = 0.0;
-  for (int64_t g0 = g_lo + threadIdx.x; g0 < g_hi; g0 += (int64_t)kReduceThreads * kReduceBatch) {
-    double v[kReduceBatch][N];
-#pragma unroll
-    for (int k = 0; k < kReduceBatch; ++k) {
-      const int64_t g = g0 + (int64_t)k * kReduceThreads;
-      const int64_t i0 = g * N;
-      if (vec && g < g_hi && i0 + N <= B) {
-        Vec16<T>::load(loss + i0, v[k]);
-      } else {
-#pragma unroll
-        for (int j = 0; j < N; ++j) v[k][j] = (g < g_hi && i0 + j < B) ? (double)loss[i0 + j] : 0.0;
-      }
-    }
-#pragma unroll
-    for (int k = 0; k < kReduceBatch; ++k)
-#pragma unroll
-      for (int j = 0; j < N; ++j) s += v[k][j];
-  }
+  double s = thread_loss_sum<T>(loss, B, g_lo, g_hi, vec);
   s = warp_sum(s);
   if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
   __syncthreads();

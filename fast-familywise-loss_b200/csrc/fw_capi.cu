@@ -162,6 +162,7 @@ const char* fw_error_string(int code) {
     case FWB_E_LAUNCH: return "CUDA kernel launch failed";
     case FWB_E_CAPACITY: return "size exceeds the stated maximum";
     case FWB_E_DTYPE: return "unsupported element type code";
+    case FWB_E_CUDA: return "a CUDA runtime call failed (allocation, IPC mapping or synchronisation)";
     default: return "unknown error";
   }
 }

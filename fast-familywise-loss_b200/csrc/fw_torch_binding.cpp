@@ -14,7 +14,8 @@
 //   * candidate_buffer/indices rows hold exactly the support (kappa entries),
 //     so fw_backward needs no zero-initialised [N,K] buffer.
 // Extra functions used by the autograd layer (fwloss_b200 package):
-//   fused_fwd_bwd, forward_rows, scale_grad, loss_reduce, shard_scan, shard_solve, and the
+//   fused_fwd_bwd, forward_rows, scale_grad, loss_reduce, loss_allreduce and its exchange
+//   buffers (peer_buffer_*), shard_scan, shard_solve, and the
 //   LM-head pieces shard_scan_into, label_logits, lmhead_fused_scan, chunks_solve,
 //   sparse_grad_hidden, sparse_grad_weight.
 #include <torch/extension.h>
@@ -359,6 +360,55 @@ torch::Tensor loss_reduce(torch::Tensor losses, double scale) {
   return out;
 }
 
+// Cross-GPU loss sum over peer memory (one process per GPU): 0-d
+// scale * (sum of every rank's losses), the same value on every rank.  bufs:
+// the world exchange buffers in rank order as mapped in this process (this
+// rank's own at index `rank`), from peer_buffer_create / peer_buffer_open.
+torch::Tensor loss_allreduce(torch::Tensor losses, double scale, std::vector<int64_t> bufs, int64_t rank,
+                             c10::optional<torch::Tensor> status, double timeout_s) {
+  TORCH_CHECK(losses.is_cuda() && losses.dim() == 1 &&
+                  (losses.scalar_type() == torch::kFloat32 || losses.scalar_type() == torch::kFloat64),
+              "losses must be a float32 or float64 CUDA vector");
+  const c10::cuda::CUDAGuard guard(losses.device());
+  auto l = losses.contiguous();
+  auto out = torch::empty({}, l.options());
+  std::vector<void*> ptrs;
+  for (int64_t b : bufs) ptrs.push_back(reinterpret_cast<void*>(b));
+  int32_t* st = nullptr;
+  if (status.has_value()) {
+    TORCH_CHECK(status->is_cuda() && status->scalar_type() == torch::kInt32 && status->numel() >= 1,
+                "status must be an int32 CUDA tensor");
+    st = status->data_ptr<int32_t>();
+  }
+  if (l.scalar_type() == torch::kFloat64) {
+    check_rc(fw_loss_allreduce_f64(l.data_ptr<double>(), l.size(0), scale, ptrs.data(), (int)ptrs.size(), (int)rank,
+                                   out.data_ptr<double>(), st, timeout_s, cur_stream()),
+             "fw_loss_allreduce_f64");
+    return out;
+  }
+  check_rc(fw_loss_allreduce(l.data_ptr<float>(), l.size(0), scale, ptrs.data(), (int)ptrs.size(), (int)rank,
+                             out.data_ptr<float>(), st, timeout_s, cur_stream()),
+           "fw_loss_allreduce");
+  return out;
+}
+
+// Exchange-buffer set-up (host calls, once per rank): create on the current
+// device -> (address, IPC handle bytes); open a peer's handle -> address.
+py::tuple peer_buffer_create() {
+  void* buf = nullptr;
+  char handle[FWB_PEER_HANDLE_BYTES];
+  check_rc(fw_peer_buffer_create(&buf, handle), "fw_peer_buffer_create");
+  return py::make_tuple(reinterpret_cast<int64_t>(buf), py::bytes(handle, FWB_PEER_HANDLE_BYTES));
+}
+
+int64_t peer_buffer_open(py::bytes handle) {
+  const std::string h = handle;
+  TORCH_CHECK(h.size() == FWB_PEER_HANDLE_BYTES, "an exchange-buffer handle has ", FWB_PEER_HANDLE_BYTES, " bytes");
+  void* p = nullptr;
+  check_rc(fw_peer_buffer_open(h.data(), &p), "fw_peer_buffer_open");
+  return reinterpret_cast<int64_t>(p);
+}
+
 // Class-sharded step 1: (grad shard zero-filled, summary [B, 4+K], local_idx [B, K]).
 std::vector<torch::Tensor> shard_scan(torch::Tensor z_local, int64_t K) {
   check_logits(z_local);
@@ -629,6 +679,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("status") = py::none());
   m.def("scale_grad_cols", &scale_grad_cols, "in-place grad scaling touching only the listed support");
   m.def("loss_reduce", &loss_reduce, "deterministic scale * sum(losses)");
+  m.def("loss_allreduce", &loss_allreduce, "scale * sum of every rank's losses, over peer memory",
+        py::arg("losses"), py::arg("scale"), py::arg("bufs"), py::arg("rank"), py::arg("status") = py::none(),
+        py::arg("timeout_s") = 10.0);
+  m.def("peer_buffer_create", &peer_buffer_create, "this rank's exchange buffer: (address, IPC handle)");
+  m.def("peer_buffer_open", &peer_buffer_open, "maps another rank's exchange buffer from its handle");
+  m.def("peer_buffer_close", [](int64_t p) { check_rc(fw_peer_buffer_close(reinterpret_cast<void*>(p)), "fw_peer_buffer_close"); });
+  m.def("peer_buffer_destroy", [](int64_t p) { check_rc(fw_peer_buffer_destroy(reinterpret_cast<void*>(p)), "fw_peer_buffer_destroy"); });
   m.def("shard_scan", &shard_scan, "class-sharded step 1: local solve, zero gradient shard, summaries");
   m.def("shard_scan_into", &shard_scan_into, "summaries of one logit chunk into given buffers");
   m.def("label_logits", &label_logits, "zy[r] = chunk[r, y[r] - c0] for labels inside the chunk");

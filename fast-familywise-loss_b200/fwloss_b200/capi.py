@@ -66,6 +66,14 @@ _SIGS["fw_forward_rows"] = ([ctypes.c_int, _P, _P, _I64, _I64, _I64, _P, _P, _P,
 _SIGS["fw_forward_rows_f64"] = ([_P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P], ctypes.c_int)
 _SIGS["fw_lmhead_fused_loss_noalloc"] = ([ctypes.c_int, _P, _I64, _I64, _P, _I64, ctypes.c_int, _P, ctypes.c_int,
                                           _P, _P, _P, _P, _P, _P, _P, _P, _P], ctypes.c_int)
+_SIGS["fw_peer_buffer_create"] = ([_P, _P], ctypes.c_int)
+_SIGS["fw_peer_buffer_open"] = ([_P, _P], ctypes.c_int)
+_SIGS["fw_peer_buffer_close"] = ([_P], ctypes.c_int)
+_SIGS["fw_peer_buffer_destroy"] = ([_P], ctypes.c_int)
+_SIGS["fw_loss_allreduce"] = ([_P, _I64, ctypes.c_double, _P, ctypes.c_int, ctypes.c_int, _P, _P,
+                               ctypes.c_double, _P], ctypes.c_int)
+_SIGS["fw_loss_allreduce_f64"] = ([_P, _I64, ctypes.c_double, _P, ctypes.c_int, ctypes.c_int, _P, _P,
+                                   ctypes.c_double, _P], ctypes.c_int)
 DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 _ANY_FLOAT = (torch.float32, torch.bfloat16, torch.float16, torch.float64)
 

@@ -11,7 +11,8 @@
  * (passed as void*, NULL = legacy default stream), launches asynchronously on
  * that stream and returns an int status (FWB_OK or one of the FWB_E* codes
  * below).  Nothing here allocates device memory, synchronises the stream or
- * reads device data on the host.  Logits are fp32 row-major with row stride
+ * reads device data on the host, except the set-up calls of the cross-GPU
+ * exchange buffer (fw_peer_buffer_create / _open / _close / _destroy).  Logits are fp32 row-major with row stride
  * `ld` (elements, ld >= C); labels are int64.  Data-dependent problems that
  * only the device can see (a label outside [0, C), a non-finite row maximum)
  * are reported through the optional device word `status` (bit-or of
@@ -46,6 +47,7 @@ extern "C" {
 #define FWB_E_LAUNCH 3     /* the CUDA launch failed (cudaGetLastError)        */
 #define FWB_E_CAPACITY 4   /* a size exceeds a stated maximum                  */
 #define FWB_E_DTYPE 5      /* unknown element type code                        */
+#define FWB_E_CUDA 6       /* a CUDA runtime call of a set-up function failed  */
 
 /* Element types of logits / gradient for the *_typed entry points (the
  * arithmetic is fp32/fp64 for all of them; 16-bit values are passed as their
@@ -56,7 +58,7 @@ extern "C" {
 
 #define FWB_STATUS_LABEL_RANGE 1   /* some label y[r] is outside [0, C)          */
 #define FWB_STATUS_NONFINITE 2     /* some row maximum is NaN or +-inf           */
-#define FWB_STATUS_TIMEOUT 4       /* a bounded on-chip wait gave up (fused LM-head kernel) */
+#define FWB_STATUS_TIMEOUT 4       /* a bounded wait gave up (fused LM-head kernel, staged streaming tiles, cross-GPU loss sum) */
 
 /* Library version, "major.minor.patch". */
 FWB_API const char* fw_version(void);
@@ -381,6 +383,46 @@ FWB_API int fw_scale_grad_f64(double* grad, const double* grad_output, int per_r
  * src/cpu/fw_cpu.cpp:729-732). */
 FWB_API int fw_loss_reduce_f64(const double* loss, int64_t B, double scale, double* out,
                                void* stream);
+
+/*
+ * Cross-GPU loss sum for row-sharded data parallelism (one process per GPU,
+ * GPUs that reach each other's memory over NVLink / NVSwitch).  The
+ * reference has no multi-GPU code; this replaces the pair "fw_loss_reduce,
+ * then an all-reduce of its scalar" that sharding its row-wise loss needs,
+ * by one kernel: each rank sums its rows' losses in fp64, stores the partial
+ * into every rank's exchange buffer through peer memory, waits (bounded) for
+ * the other ranks' partials in its own buffer and writes
+ *     out[0] = scale * (partial_0 + partial_1 + ... + partial_{world-1})
+ * (fp64, rank order: every rank gets the same value).
+ *
+ * Set-up, once per rank (these allocate and synchronise):
+ *   fw_peer_buffer_create  allocates this rank's FWB_PEER_BUFFER_BYTES
+ *                          exchange buffer on the current device, zeroes it
+ *                          and returns it with its CUDA IPC handle
+ *                          (FWB_PEER_HANDLE_BYTES bytes); the host sends the
+ *                          handles to every rank (e.g. an all-gather);
+ *   fw_peer_buffer_open    maps another rank's buffer from its handle;
+ *   fw_peer_buffer_close / fw_peer_buffer_destroy  undo the two.
+ * fw_loss_allreduce(_f64) takes the world buffers in rank order (this rank's
+ * own buffer at index `rank`, the opened ones elsewhere).  Every rank must
+ * make the same sequence of calls on its buffers, each on one stream at a
+ * time (calls that overlap on one rank race).  A rank whose peers do not
+ * publish within timeout_s seconds sets FWB_STATUS_TIMEOUT in *status (if
+ * given) and writes NaN; the buffers cannot be used after that.  Returns
+ * FWB_E_CAPACITY for world > FWB_PEER_MAX.
+ */
+#define FWB_PEER_MAX 8
+#define FWB_PEER_HANDLE_BYTES 64
+#define FWB_PEER_BUFFER_BYTES 512
+FWB_API int fw_peer_buffer_create(void** buf, void* handle);
+FWB_API int fw_peer_buffer_open(const void* handle, void** peer);
+FWB_API int fw_peer_buffer_close(void* peer);
+FWB_API int fw_peer_buffer_destroy(void* buf);
+FWB_API int fw_loss_allreduce(const float* loss, int64_t B, double scale, void* const* bufs, int world,
+                              int rank, float* out, int32_t* status, double timeout_s, void* stream);
+FWB_API int fw_loss_allreduce_f64(const double* loss, int64_t B, double scale, void* const* bufs,
+                                  int world, int rank, double* out, int32_t* status, double timeout_s,
+                                  void* stream);
 
 /*
  * LM-head forward in one call that allocates nothing: fw_lmhead_fused_scan

@@ -9,8 +9,14 @@ its own GPU):
     implicit upstream gradient 1 and with an upstream factor of 3;
   * the forward-only path (torch.no_grad): the same loss;
   * the step captured once in a CUDA graph (forward kernel, loss reduction,
-    the NCCL all-reduce and the backward) and replayed on new logits, as
-    bench.py runs it.
+    the cross-GPU loss sum and the backward) and replayed on new logits, as
+    bench.py runs it;
+  * the cross-GPU loss sum over peer memory (fw_loss_allreduce) itself: used
+    whenever every pair of GPUs has peer access, equal on every rank to the
+    bit, within 1e-6 of the loss reduction + NCCL all-reduce over several
+    calls in a row (both epoch parities), fp32 and fp64 losses;
+  * its bounded wait: on a separate exchange only rank 0 calls (0.3 s limit),
+    and gets NaN and FWB_STATUS_TIMEOUT instead of waiting for good.
 
 Exits non-zero when any rank failed."""
 import datetime
@@ -24,7 +30,9 @@ import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
 from fwloss_b200 import familywise_loss, workloads  # noqa: E402
-from fwloss_b200.distributed import shard_rows, sharded_familywise_loss  # noqa: E402
+from fwloss_b200._native import ext  # noqa: E402
+from fwloss_b200.distributed import (PeerLossExchange, loss_exchange, reduce_loss_sum,  # noqa: E402
+                                     shard_rows, sharded_familywise_loss)
 
 
 def full_reference(z, y):
@@ -93,11 +101,50 @@ def main():
     del g, static_loss  # release the graph (it holds an NCCL call) before the group goes
     torch.cuda.synchronize(dev)
 
+    ok &= check_peer_sum(dev, rank, world)
+
     flag = torch.tensor([0 if ok else 1], device=dev)
     dist.all_reduce(flag)
     dist.destroy_process_group()
     print(f"rank {rank}/{world}: ok={bool(ok)}")
     sys.exit(int(flag.item() != 0))
+
+
+def check_peer_sum(dev, rank, world):
+    ok = True
+    peer_ok = all(torch.cuda.can_device_access_peer(dev.index, d) for d in range(torch.cuda.device_count())
+                  if d != dev.index)
+    ex = loss_exchange(None, dev)
+    if world > 1 and peer_ok and torch.cuda.device_count() >= world:
+        ok &= ex is not None  # the peer-memory path is the one that runs
+    if ex is None:
+        return ok
+    g = torch.Generator().manual_seed(100 + rank)
+    for i in range(5):  # epochs 1..5 of this exchange's own calls: both parities
+        for dt in (torch.float32, torch.float64):
+            losses = (torch.rand(37 + 11 * rank + i, generator=g, dtype=torch.float64) * 3).to(dt).to(dev)
+            scale = 1.0 / 1000.0
+            got = ex.reduce(losses, scale)
+            ref = reduce_loss_sum(ext().loss_reduce(losses, scale))
+            every = [torch.zeros((), dtype=dt, device=dev) for _ in range(world)]
+            dist.all_gather(every, got.reshape(()).contiguous())
+            ok &= all(bool(torch.equal(e, every[0])) for e in every)
+            ok &= abs(float(got) - float(ref)) <= 1e-6 * max(1.0, abs(float(ref)))
+    torch.cuda.synchronize(dev)
+    ex.check()
+
+    # bounded wait: a second exchange on which only rank 0 calls
+    solo = PeerLossExchange(None, dev, timeout_s=0.3)
+    if solo.available:
+        if rank == 0:
+            out = solo.reduce(torch.ones(8, device=dev), 1.0)
+            torch.cuda.synchronize(dev)
+            if world > 1:
+                ok &= bool(torch.isnan(out)) and int(solo.status.item()) == 4
+            else:
+                ok &= float(out) == 8.0 and int(solo.status.item()) == 0
+        solo.close()
+    return ok
 
 
 if __name__ == "__main__":

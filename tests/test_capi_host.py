@@ -38,7 +38,7 @@ def test_only_c_abi_is_exported():
 def test_version_and_error_strings():
     assert capi.version() == "0.1.0"
     lib = capi.load()
-    for code in range(5):
+    for code in range(7):
         assert lib.fw_error_string(code)
     assert b"unknown" in lib.fw_error_string(99)
 
@@ -120,3 +120,26 @@ def test_argument_checks_of_the_later_entry_points():
     # nchunks * K above the chunk solve's 256-entry list: refused before any kernel is queued
     cs16 = (ctypes.c_int64 * 17)(*[256 * i for i in range(17)])
     assert lib.fw_lmhead_fused_loss_noalloc(1, d, 4, 64, d, 4096, 16, cs16, 32, d, P, d, P, d, d, d, P, P) == 4
+
+
+def test_argument_checks_of_the_cross_gpu_loss_sum():
+    """fw_loss_allreduce refuses bad rank counts, ranks, pointers and timeouts
+    before any device work; the exchange-buffer set-up refuses null
+    pointers."""
+    lib = capi.load()
+    P = None
+    d = ctypes.c_void_p(256)
+    bufs = (ctypes.c_void_p * 9)(*([256] * 9))
+    assert lib.fw_loss_allreduce(d, 4, 1.0, bufs, 9, 0, d, P, 1.0, P) == 4     # world > FWB_PEER_MAX
+    assert lib.fw_loss_allreduce(d, 4, 1.0, bufs, 0, 0, d, P, 1.0, P) == 4     # world < 1
+    assert lib.fw_loss_allreduce(d, 4, 1.0, bufs, 2, 2, d, P, 1.0, P) == 1     # rank outside [0, world)
+    assert lib.fw_loss_allreduce(d, -1, 1.0, bufs, 2, 0, d, P, 1.0, P) == 1    # B < 0
+    assert lib.fw_loss_allreduce(d, 4, 1.0, bufs, 2, 0, d, P, 0.0, P) == 1     # timeout must be > 0
+    assert lib.fw_loss_allreduce(d, 4, 1.0, bufs, 2, 0, P, P, 1.0, P) == 2     # out
+    assert lib.fw_loss_allreduce(P, 4, 1.0, bufs, 2, 0, d, P, 1.0, P) == 2     # losses
+    holes = (ctypes.c_void_p * 2)(256, None)
+    assert lib.fw_loss_allreduce_f64(d, 4, 1.0, holes, 2, 0, d, P, 1.0, P) == 2  # a missing buffer
+    assert lib.fw_peer_buffer_create(P, d) == 2
+    assert lib.fw_peer_buffer_open(P, d) == 2
+    assert lib.fw_peer_buffer_close(P) == 2
+    assert lib.fw_peer_buffer_destroy(P) == 2
