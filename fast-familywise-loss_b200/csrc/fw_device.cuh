@@ -14,6 +14,8 @@
 //           S_k - 1 would lose the 1 entirely.
 #pragma once
 
+#include <type_traits>
+
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -99,6 +101,14 @@ __device__ __forceinline__ uint4 pack16(const float* in) {
   }
 }
 
+// A 16-byte slot of -inf elements (padding past the end of a segment).
+template <class T>
+__device__ __forceinline__ uint4 neg_inf_slot() {
+  constexpr uint32_t w = sizeof(T) == 4 ? 0xff800000u
+                                        : (std::is_same<T, __nv_bfloat16>::value ? 0xff80ff80u : 0xfc00fc00u);
+  return make_uint4(w, w, w, w);
+}
+
 // Streaming 16-byte load that does not pollute L1.
 __device__ __forceinline__ uint4 ld_stream16(const void* p) {
   uint4 r;
@@ -150,6 +160,31 @@ __device__ __forceinline__ float max_nan(float a, float b) {
   asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
   return r;
 }
+
+// Largest element of a 16-byte slot as fp32, NaN when any element is NaN:
+// three max.NaN for fp32; for 16-bit types three packed max.NaN on element
+// pairs, then the larger of the two halves (an exact selection, so the same
+// value as the fp32 max over the unpacked elements up to the sign of a zero).
+template <class T>
+__device__ __forceinline__ float slot_max_nan(const uint4& u) {
+  if constexpr (sizeof(T) == 4) {
+    return max_nan(max_nan(__uint_as_float(u.x), __uint_as_float(u.y)),
+                   max_nan(__uint_as_float(u.z), __uint_as_float(u.w)));
+  } else {
+    uint32_t a, b, c;
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(a) : "r"(u.x), "r"(u.y));
+      asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(b) : "r"(u.z), "r"(u.w));
+      asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(c) : "r"(a), "r"(b));
+    } else {
+      asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(a) : "r"(u.x), "r"(u.y));
+      asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(b) : "r"(u.z), "r"(u.w));
+      asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(c) : "r"(a), "r"(b));
+    }
+    return max_nan(Elem<T>::bits_to_f(c & 0xffffu), Elem<T>::bits_to_f(c >> 16));
+  }
+}
+
 
 // Order-preserving fp32 -> uint32 key.  -0.0 is folded onto +0.0 first, so
 // that keys order exactly like the float comparison used for selection

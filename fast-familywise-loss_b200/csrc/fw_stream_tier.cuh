@@ -345,42 +345,36 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a,
 
   // One streaming step: this thread's IPT items base + u * NT + tid (values
   // in v, -inf past the segment): zero output, running max, candidates.
-  auto consume = [&](float (&v)[IPT * W], int64_t base) {
+  // Outputs of one item that need no values: the zero gradient (or mask).
+  auto zero_item = [&](int64_t it) {
+    if (it < g.i1) {
+      if (kZeroFill && (OUT == kOutGrad || gr != nullptr)) {
+        if (VEC)
+          *reinterpret_cast<uint4*>(gr + W * it) = make_uint4(0u, 0u, 0u, 0u);
+        else
+          st_elem(gr + it, 0.0f);
+      } else if (OUT == kOutMask) {
+        if (VEC && a.mask_vec)
+          *reinterpret_cast<uchar4*>(mr + 4 * it) = make_uchar4(0, 0, 0, 0);
+        else
 #pragma unroll
-    for (int u = 0; u < IPT; ++u) {
-      const int64_t it = base + (int64_t)u * NT + tid;
-      if ((int)it == y_item) {  // rare: this item holds the label column
-        const int jy = yc - y_item * W;
-#pragma unroll
-        for (int j = 0; j < W; ++j)
-          if (j == jy) s.label_z = v[u * W + j];
-      }
-      if (it < g.i1) {
-        if (kZeroFill && (OUT == kOutGrad || gr != nullptr)) {
-          if (VEC)
-            *reinterpret_cast<uint4*>(gr + W * it) = make_uint4(0u, 0u, 0u, 0u);
-          else
-            st_elem(gr + it, 0.0f);
-        } else if (OUT == kOutMask) {
-          if (VEC && a.mask_vec)
-            *reinterpret_cast<uchar4*>(mr + 4 * it) = make_uchar4(0, 0, 0, 0);
-          else
-#pragma unroll
-            for (int j = 0; j < W; ++j) mr[it * W + j] = 0;
-        }
+          for (int j = 0; j < W; ++j) mr[it * W + j] = 0;
       }
     }
-    float m = -CUDART_INF_F;
-#pragma unroll
-    for (int k = 0; k < IPT * W; ++k) m = max_nan(m, v[k]);
+  };
+  // The step's warp maximum joins the running maximum (shared across the
+  // CTA's warps); returns the step's candidate threshold.
+  auto step_threshold = [&](float m) -> float {
     m = warp_max_nan(m);
     run = max_nan(run, m);
     if (lane == 0) atomicMax(&s.run_key, sort_key(run));
     const float shared_max = key_value(*reinterpret_cast<volatile unsigned*>(&s.run_key));
-    const float t = __fsub_rd(fmaxf(run, shared_max), 1.0f);
-    // candidates of this step: one count per lane, one warp scan for the
-    // offsets, then every lane stores its own in element order (the list
-    // holds them lane-major; a fixed order, so the solve stays deterministic)
+    return __fsub_rd(fmaxf(run, shared_max), 1.0f);
+  };
+  // Candidates of one step: one count per lane, one warp scan for the
+  // offsets, then every lane stores its own in element order (the list holds
+  // them lane-major; a fixed order, so the solve stays deterministic).
+  auto candidates = [&](float (&v)[IPT * W], int64_t base, float t) {
     int c = 0;
 #pragma unroll
     for (int k = 0; k < IPT * W; ++k) c += (v[k] > t) ? 1 : 0;
@@ -407,6 +401,60 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a,
         }
         wcnt += total;
       }
+    }
+  };
+  // One streaming step over element values (rows without 16-byte loads):
+  // label, zero output, running max, candidates.
+  auto consume = [&](float (&v)[IPT * W], int64_t base) {
+#pragma unroll
+    for (int u = 0; u < IPT; ++u) {
+      const int64_t it = base + (int64_t)u * NT + tid;
+      if ((int)it == y_item) {  // rare: this item holds the label column
+        const int jy = yc - y_item * W;
+#pragma unroll
+        for (int j = 0; j < W; ++j)
+          if (j == jy) s.label_z = v[u * W + j];
+      }
+      zero_item(it);
+    }
+    float m = -CUDART_INF_F;
+#pragma unroll
+    for (int k = 0; k < IPT * W; ++k) m = max_nan(m, v[k]);
+    candidates(v, base, step_threshold(m));
+  };
+  // One streaming step over 16-byte slots (q: this thread's IPT slots, -inf
+  // past the segment): each slot is reduced to its maximum first (packed
+  // pairs for 16-bit types), and the elements are unpacked and counted only
+  // when some lane of the warp has a slot above the step's threshold --
+  // rarely, since candidates lie within 1 of the row maximum.
+  auto consume_slots = [&](const uint4 (&q)[IPT], int64_t base) {
+    float im[IPT];
+#pragma unroll
+    for (int u = 0; u < IPT; ++u) {
+      const int64_t it = base + (int64_t)u * NT + tid;
+      if ((int)it == y_item) {  // rare: this item holds the label column
+        float e[W];
+        unpack16<T>(q[u], e);
+        const int jy = yc - y_item * W;
+#pragma unroll
+        for (int j = 0; j < W; ++j)
+          if (j == jy) s.label_z = e[j];
+      }
+      zero_item(it);
+      im[u] = slot_max_nan<T>(q[u]);
+    }
+    float m = im[0];
+#pragma unroll
+    for (int u = 1; u < IPT; ++u) m = max_nan(m, im[u]);
+    const float t = step_threshold(m);
+    bool hit = false;
+#pragma unroll
+    for (int u = 0; u < IPT; ++u) hit |= im[u] > t;
+    if (__any_sync(kFull, hit)) {
+      float v[IPT * W];
+#pragma unroll
+      for (int u = 0; u < IPT; ++u) unpack16<T>(q[u], &v[u * W]);
+      candidates(v, base, t);
     }
   };
 
@@ -440,18 +488,13 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a,
         if (!ok) s.stage_abort = 1;
       }
       const uint4* tile = stream_ring + (size_t)st * kStageItems;
-      float v[IPT * W];
+      uint4 q[IPT];
 #pragma unroll
       for (int u = 0; u < IPT; ++u) {
         const int l = u * NT + tid;
-        if (ok && base + l < g.i1) {
-          unpack16<T>(tile[l], &v[W * u]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < W; ++j) v[W * u + j] = -CUDART_INF_F;
-        }
+        q[u] = (ok && base + l < g.i1) ? tile[l] : neg_inf_slot<T>();
       }
-      consume(v, base);
+      consume_slots(q, base);
       __syncthreads();  // every thread is done with this stage
       aborted = s.stage_abort != 0;
       if (tid == 0 && !aborted && issued < ntiles) issue(issued++);
@@ -466,22 +509,23 @@ __device__ __forceinline__ void stream_rows_body(const RowArgs& a,
         if (last >= 0) mbar_wait_for(&s.stage_full[st], (uint32_t)(last / kStages) & 1u, kStageDrainLimitNs);
       }
     }
+  } else if constexpr (VEC) {
+    for (int64_t base = g.i0; base < g.i1; base += (int64_t)NT * IPT) {
+      uint4 q[IPT];
+#pragma unroll
+      for (int u = 0; u < IPT; ++u) {
+        const int64_t it = base + (int64_t)u * NT + tid;
+        q[u] = (it < g.i1) ? ld_stream16(zr + W * it) : neg_inf_slot<T>();
+      }
+      consume_slots(q, base);
+    }
   } else {
     for (int64_t base = g.i0; base < g.i1; base += (int64_t)NT * IPT) {
       float v[IPT * W];
 #pragma unroll
       for (int u = 0; u < IPT; ++u) {
         const int64_t it = base + (int64_t)u * NT + tid;
-        if (VEC) {
-          if (it < g.i1) {
-            unpack16<T>(ld_stream16(zr + W * it), &v[W * u]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < W; ++j) v[W * u + j] = -CUDART_INF_F;
-          }
-        } else {
-          v[u] = (it < g.i1) ? ld_elem(zr + it) : -CUDART_INF_F;
-        }
+        v[u] = (it < g.i1) ? ld_elem(zr + it) : -CUDART_INF_F;
       }
       consume(v, base);
     }
