@@ -8,8 +8,10 @@
 //   1. load (16-byte loads when rows are 16-byte aligned), M = NaN-propagating
 //      max by xor shuffles inside the group;
 //   2. n = |{z > t0}|; a unique maximum (n == 1) is solved on the spot
-//      (kappa = 1, h* = M - 1); otherwise the candidates are compacted into a
-//      per-group list by an exclusive shuffle scan;
+//      (kappa = 1, h* = M - 1), and so are more than G candidates that all
+//      equal M (kappa = n, h* = M - 1/n; rows of up to 16 values per lane);
+//      otherwise the candidates are
+//      compacted into a per-group list by an exclusive shuffle scan;
 //   3. exact threshold: Michelot's fixed point with one candidate per lane
 //      when there are at most G of them (michelot_lane: counts are a
 //      ballot), on the list otherwise (michelot_list), or on the registers
@@ -170,7 +172,7 @@ __device__ __forceinline__ void warp_tier_nonfinite(const RowArgs& a, int64_t ro
 // issue-bound (a serial chain per row: load, max, solve, write), so the
 // budgets keep every row of a few-thousand-row batch resident at once:
 //   NV <= 16   256 threads x 4 CTAs (64 registers);
-//   NV == 32   128 threads x 7 CTAs (73 registers, no spills): 4144 resident
+//   NV == 32   128 threads x 7 CTAs (73 registers): 4144 resident
 //              warps on 148 SMs, one per row of a 4096-row batch;
 //   NV == 64   256 threads x 1 CTA.
 template <int NV>
@@ -260,10 +262,26 @@ __global__ void __launch_bounds__(warp_tier_threads<NS * Elem<T>::kEPS>(),
     const int n = group_sum<G>(c, gmask);
     double tau;
     int kap;
+    // More candidates than lanes: are they all equal to the maximum (ties of
+    // quantized logits)?  Then the fixed point ends at its first step,
+    // kappa = n and h* = M - 1/n (sum of z - M over the set is 0; bit-equal
+    // to what the list form computes), without the list.  Checked with at
+    // most 16 values per lane (the 32-value instance has no registers left
+    // for it under its 7-CTAs-per-SM budget).
+    bool ties = false;
+    if (NV <= 16 && n > G) {
+      int e = 0;
+#pragma unroll
+      for (int s = 0; s < NV; ++s) e += (v[s] == m) ? 1 : 0;
+      ties = group_sum<G>(e, gmask) == n;
+    }
     if (n == 1) {
       // a unique maximum and nothing else above M - 1: h* = M - 1, kappa = 1
       tau = -1.0;
       kap = 1;
+    } else if (ties) {
+      tau = (0.0 - 1.0) / (double)n;
+      kap = n;
     } else if (n <= CAPG) {
       int off = group_excl_scan<G>(c, li, gmask);
       if (c > 0) {
