@@ -105,7 +105,8 @@ def _worker_autograd(rank, world, port, B, C, out):
     (loss * 3.0).backward()
     with torch.no_grad():
         nograd = D.sharded_familywise_loss(zl, yl, B)
-    out[rank] = (float(loss), zl.grad.numpy().copy(), a, b, float(nograd), list(fake.calls))
+    no_exchange = D.loss_exchange() is None  # gloo: the loss sum is reduction + all-reduce
+    out[rank] = (float(loss), zl.grad.numpy().copy(), a, b, float(nograd), list(fake.calls), no_exchange)
     dist.barrier()
     dist.destroy_process_group()
 
@@ -115,7 +116,8 @@ def test_sharded_autograd_function_host_logic(world):
     """sharded_familywise_loss forward/backward under gloo with the kernel
     calls stubbed: every rank returns the global mean loss, its rows of the
     global gradient times the upstream factor, the fused kernel runs with the
-    global scale 1/B, and the no-grad call takes the forward-only kernel."""
+    global scale 1/B, the no-grad call takes the forward-only kernel, and a
+    gloo group sums the loss by reduction + all-reduce (no peer exchange)."""
     B, C = 29, 150
     mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
@@ -129,7 +131,8 @@ def test_sharded_autograd_function_host_logic(world):
     full = O.solve(z, y, 1.0 / B)
     mean = full["loss"].mean()
     for r in range(world):
-        loss, g, a, b, nograd, calls = out[r]
+        loss, g, a, b, nograd, calls, no_exchange = out[r]
+        assert no_exchange
         np.testing.assert_allclose(loss, mean, rtol=1e-6)
         np.testing.assert_allclose(nograd, mean, rtol=1e-6)
         np.testing.assert_allclose(g, 3.0 * full["grad"][a:b], rtol=1e-6, atol=1e-9)
